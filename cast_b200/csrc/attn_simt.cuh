@@ -1,0 +1,325 @@
+// Split-KV CUDA-core tree attention (any dtype, head dim 64/128, any pack size).
+//
+// This is the exact-fp32 path: q/k/v are widened to fp32 in shared memory and
+// every product is an fp32 FMA, so fp32 inputs meet a 1e-4 bound against the
+// fp32 oracle. It also serves fp16 inputs and any shape the tensor-core kernel
+// does not take.
+//
+// Work unit (one CTA): sequence b, KV head h, a 64-row tile of the G*P_b query
+// rows of that head group (row r = token r / G, query head h*G + r % G), and a
+// chunk of the key range [0, S_b + P_b). Keys < S_b are the prefix and always
+// visible; key S_b + j is pack token j, visible iff bit j of the row token's
+// ancestor bitset is set (cast_trees/tree_attn.py:50-87). The bitsets of the
+// tile's tokens live in shared memory, built from `parent` or copied from the
+// caller's words. With one key chunk the CTA writes the output; with several
+// it writes fp32 partials (unnormalised O, running max m in log2 units, sum l)
+// that attn_combine_kernel merges.
+#pragma once
+
+#include "common.cuh"
+
+namespace cast {
+
+struct AttnParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int64_t sq_m, sq_h, sk_m, sk_h, sv_m, sv_h, so_m, so_h;
+  const int32_t* cu_q;
+  const int32_t* cu_kv;
+  const int32_t* prefix_len;
+  const int32_t* pack_len;
+  const int64_t* anc_words;
+  int anc_wpr;
+  const int32_t* parent;
+  int B, total_q, total_kv, H_q, H_kv, G, D;
+  float scale_log2;
+  int max_pack, max_kv;
+  int n_split, chunk, m_tiles, W;
+  float* ws_o;   // [n_split, total_q, H_q, D]
+  float* ws_ml;  // [n_split, total_q, H_q, 2]
+};
+
+namespace simt {
+constexpr int BM = 64, BN = 64, NT = 256;
+template <int D> __host__ __device__ constexpr int qk_stride() { return D + 4; }
+template <int D> __host__ __device__ constexpr size_t smem_bytes(int W) {
+  return sizeof(float) * (2 * BM * qk_stride<D>() + BN * D + BM * (BN + 1)) +
+         sizeof(uint64_t) * (BM + 1) * W;
+}
+}  // namespace simt
+
+// Builds the ancestor bitsets of pack tokens [i_lo, i_lo + nt) into s_anc
+// ([nt][W] words). One thread per token; each walks its own ancestor chain
+// (parent[j] < j, so the walk ends within j + 1 steps).
+__device__ __forceinline__ void build_tile_bitsets(const AttnParams& p, const SeqMeta& m, int i_lo,
+                                                   int nt, uint64_t* s_anc) {
+  const int W = p.W;
+  const int wn = (m.P + 63) >> 6;
+  for (int li = threadIdx.x; li < nt; li += blockDim.x) {
+    uint64_t* row = s_anc + (size_t)li * W;
+    for (int w = 0; w < W; ++w) row[w] = 0ull;
+    const int i = i_lo + li;
+    if (p.anc_words != nullptr) {
+      const int64_t* src = p.anc_words + (int64_t)(m.q0 + i) * p.anc_wpr;
+      const int wc = min(wn, p.anc_wpr);
+      for (int w = 0; w < wc; ++w) row[w] = (uint64_t)src[w];
+    } else {
+      int j = i;
+      int guard = 0;
+      while (j >= 0 && guard <= i) {
+        row[j >> 6] |= 1ull << (j & 63);
+        const int pj = p.parent[m.q0 + j];
+        if (pj >= j || pj < -1 || (j == 0 && pj != -1)) {
+          report(CAST_DEV_BAD_PARENT);
+          break;
+        }
+        j = pj;
+        ++guard;
+      }
+    }
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(simt::NT)
+attn_simt_kernel(const AttnParams p) {
+  using namespace simt;
+  constexpr int QS = qk_stride<D>();
+  constexpr int CPT = D / 16;  // output columns per thread (4 or 8)
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* sQ = reinterpret_cast<float*>(smem_raw);
+  float* sK = sQ + BM * QS;
+  float* sV = sK + BN * QS;
+  float* sP = sV + BN * D;
+  uint64_t* sAnc = reinterpret_cast<uint64_t*>(sP + BM * (BN + 1));
+
+  const int tid = threadIdx.x;
+  const int ty = tid >> 4, tx = tid & 15;
+  const int b = blockIdx.y / p.H_kv, h = blockIdx.y % p.H_kv;
+  const SeqMeta m = load_seq(p.cu_q, p.cu_kv, p.prefix_len, p.pack_len, b, p.total_q, p.total_kv,
+                             p.max_pack, p.max_kv);
+  if (!m.ok) {
+    if (tid == 0 && blockIdx.x == 0 && blockIdx.z == 0) report(CAST_DEV_BAD_LAYOUT);
+    return;
+  }
+  const int G = p.G;
+  const int rows = G * m.P;
+  const int r0 = blockIdx.x * BM;
+  if (r0 >= rows) return;
+  const int nkeys = m.S + m.P;
+  const int k_begin = blockIdx.z * p.chunk;
+  if (k_begin >= nkeys) return;
+  const int k_end = min(nkeys, k_begin + p.chunk);
+
+  const T* Q = static_cast<const T*>(p.q);
+  const T* K = static_cast<const T*>(p.k);
+  const T* V = static_cast<const T*>(p.v);
+
+  // Q tile, pre-scaled into log2 units; rows past the pack are zero.
+  for (int e = tid; e < BM * (D / 4); e += NT) {
+    const int rr = e / (D / 4), c4 = (e % (D / 4)) * 4;
+    const int r = r0 + rr;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < rows) {
+      const int i = r / G, g = r % G;
+      x = load4<T>(Q + (int64_t)(m.q0 + i) * p.sq_m + (int64_t)(h * G + g) * p.sq_h + c4);
+      x.x *= p.scale_log2; x.y *= p.scale_log2; x.z *= p.scale_log2; x.w *= p.scale_log2;
+    }
+    *reinterpret_cast<float4*>(sQ + rr * QS + c4) = x;
+  }
+  const int i_lo = r0 / G;
+  const int i_hi = min(m.P - 1, (r0 + BM - 1) / G);
+  if (k_end > m.S) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc);
+
+  float o[4][CPT];
+  float mrow[4], lrow[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    mrow[a] = -INFINITY;
+    lrow[a] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) o[a][c] = 0.f;
+  }
+
+  for (int kb = k_begin; kb < k_end; kb += BN) {
+    __syncthreads();  // previous tile's sK/sV/sP reads are done (and sQ/sAnc writes on entry)
+    for (int e = tid; e < BN * (D / 4); e += NT) {
+      const int rr = e / (D / 4), c4 = (e % (D / 4)) * 4;
+      const int n = kb + rr;
+      float4 kx = make_float4(0.f, 0.f, 0.f, 0.f), vx = kx;
+      if (n < k_end) {
+        const int64_t row = m.kv0 + n;
+        kx = load4<T>(K + row * p.sk_m + (int64_t)h * p.sk_h + c4);
+        vx = load4<T>(V + row * p.sv_m + (int64_t)h * p.sv_h + c4);
+      }
+      *reinterpret_cast<float4*>(sK + rr * QS + c4) = kx;
+      *reinterpret_cast<float4*>(sV + rr * D + c4) = vx;
+    }
+    __syncthreads();
+
+    float s[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[a][c] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < D; d += 4) {
+      float4 qa[4], kc[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(sQ + (ty + 16 * a) * QS + d);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) kc[c] = *reinterpret_cast<const float4*>(sK + (tx + 16 * c) * QS + d);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          s[a][c] = fmaf(qa[a].x, kc[c].x, s[a][c]);
+          s[a][c] = fmaf(qa[a].y, kc[c].y, s[a][c]);
+          s[a][c] = fmaf(qa[a].z, kc[c].z, s[a][c]);
+          s[a][c] = fmaf(qa[a].w, kc[c].w, s[a][c]);
+        }
+    }
+
+    // visibility: prefix keys always, pack keys by ancestor bit, nothing past k_end
+    const bool full = (kb + BN <= m.S) && (kb + BN <= k_end);
+    if (!full) {
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const int r = r0 + ty + 16 * a;
+        const int li = min(r / G, m.P - 1) - i_lo;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int n = kb + tx + 16 * c;
+          bool vis = n < k_end;
+          if (vis && n >= m.S) {
+            const int j = n - m.S;
+            vis = (sAnc[(size_t)li * p.W + (j >> 6)] >> (j & 63)) & 1ull;
+          }
+          if (!vis) s[a][c] = -INFINITY;
+        }
+      }
+    }
+
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      float mx = fmaxf(fmaxf(s[a][0], s[a][1]), fmaxf(s[a][2], s[a][3]));
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off, 16));
+      const float m_new = fmaxf(mrow[a], mx);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = exp2f(mrow[a] - m_use);
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float pv = exp2f(s[a][c] - m_use);
+        rs += pv;
+        sP[(ty + 16 * a) * (BN + 1) + tx + 16 * c] = pv;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off, 16);
+      lrow[a] = lrow[a] * alpha + rs;
+      mrow[a] = m_new;
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) o[a][c] *= alpha;
+    }
+    __syncthreads();
+
+#pragma unroll 4
+    for (int kk = 0; kk < BN; ++kk) {
+      float4 v0 = *reinterpret_cast<const float4*>(sV + kk * D + tx * 4);
+      float4 v1 = v0;
+      if constexpr (CPT == 8) v1 = *reinterpret_cast<const float4*>(sV + kk * D + 64 + tx * 4);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const float pa = sP[(ty + 16 * a) * (BN + 1) + kk];
+        o[a][0] = fmaf(pa, v0.x, o[a][0]);
+        o[a][1] = fmaf(pa, v0.y, o[a][1]);
+        o[a][2] = fmaf(pa, v0.z, o[a][2]);
+        o[a][3] = fmaf(pa, v0.w, o[a][3]);
+        if constexpr (CPT == 8) {
+          o[a][4] = fmaf(pa, v1.x, o[a][4]);
+          o[a][5] = fmaf(pa, v1.y, o[a][5]);
+          o[a][6] = fmaf(pa, v1.z, o[a][6]);
+          o[a][7] = fmaf(pa, v1.w, o[a][7]);
+        }
+      }
+    }
+  }
+
+  // epilogue: each of the 16 threads of a row holds CPT of its D columns
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int r = r0 + ty + 16 * a;
+    if (r >= rows) continue;
+    const int i = r / G, hq = h * G + r % G;
+    const int64_t t = m.q0 + i;
+    if (p.n_split == 1) {
+      const float inv = lrow[a] > 0.f ? 1.f / lrow[a] : 0.f;
+      T* O = static_cast<T*>(p.out) + t * p.so_m + (int64_t)hq * p.so_h;
+      store4<T>(O + tx * 4, make_float4(o[a][0] * inv, o[a][1] * inv, o[a][2] * inv, o[a][3] * inv));
+      if constexpr (CPT == 8)
+        store4<T>(O + 64 + tx * 4, make_float4(o[a][4] * inv, o[a][5] * inv, o[a][6] * inv, o[a][7] * inv));
+    } else {
+      const int64_t slot = ((int64_t)blockIdx.z * p.total_q + t) * p.H_q + hq;
+      float* O = p.ws_o + slot * D;
+      *reinterpret_cast<float4*>(O + tx * 4) = make_float4(o[a][0], o[a][1], o[a][2], o[a][3]);
+      if constexpr (CPT == 8)
+        *reinterpret_cast<float4*>(O + 64 + tx * 4) = make_float4(o[a][4], o[a][5], o[a][6], o[a][7]);
+      if (tx == 0) {
+        p.ws_ml[slot * 2 + 0] = mrow[a];
+        p.ws_ml[slot * 2 + 1] = lrow[a];
+      }
+    }
+  }
+}
+
+// Merges the key-chunk partials of one (query row, query head) per warp.
+template <typename T>
+__global__ void __launch_bounds__(256) attn_combine_kernel(const AttnParams p) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= p.total_q * p.H_q) return;
+  const int t = warp / p.H_q, hq = warp % p.H_q;
+  // sequence of row t: last b with cu_q[b] <= t
+  int lo = 0, hi = p.B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.cu_q[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  const int b = lo;
+  const SeqMeta m = load_seq(p.cu_q, p.cu_kv, p.prefix_len, p.pack_len, b, p.total_q, p.total_kv,
+                             p.max_pack, p.max_kv);
+  if (!m.ok || t < m.q0 || t >= m.q0 + m.P) return;
+  const int nsplit = min(p.n_split, (m.S + m.P + p.chunk - 1) / p.chunk);
+  float M = -INFINITY;
+  for (int z = 0; z < nsplit; ++z)
+    M = fmaxf(M, p.ws_ml[(((int64_t)z * p.total_q + t) * p.H_q + hq) * 2]);
+  const float m_use = (M == -INFINITY) ? 0.f : M;
+  float L = 0.f;
+  float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  const int nv = p.D / 128 + (p.D % 128 ? 1 : 0);  // float4 groups per lane: D/128 (1 for D=64 uses half the lanes)
+  for (int z = 0; z < nsplit; ++z) {
+    const int64_t slot = ((int64_t)z * p.total_q + t) * p.H_q + hq;
+    const float w = exp2f(p.ws_ml[slot * 2] - m_use);
+    L += w * p.ws_ml[slot * 2 + 1];
+    const float* O = p.ws_o + slot * p.D;
+    for (int g = 0; g < nv; ++g) {
+      const int c = (g * 32 + lane) * 4;
+      if (c < p.D) {
+        const float4 x = *reinterpret_cast<const float4*>(O + c);
+        acc[g].x += w * x.x; acc[g].y += w * x.y; acc[g].z += w * x.z; acc[g].w += w * x.w;
+      }
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  T* out = static_cast<T*>(p.out) + (int64_t)t * p.so_m + (int64_t)hq * p.so_h;
+  for (int g = 0; g < nv; ++g) {
+    const int c = (g * 32 + lane) * 4;
+    if (c < p.D)
+      store4<T>(out + c, make_float4(acc[g].x * inv, acc[g].y * inv, acc[g].z * inv, acc[g].w * inv));
+  }
+}
+
+}  // namespace cast

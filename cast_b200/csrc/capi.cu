@@ -1,0 +1,241 @@
+// C ABI of cast_b200 (declared in include/cast_b200.h): argument checks, launch
+// planning and kernel dispatch. Everything the library launches is in this
+// translation unit, so the per-device error word is one symbol.
+#include <math.h>
+#include <stdio.h>
+#include <atomic>
+
+#include "common.cuh"
+#include "attn_simt.cuh"
+#include "tree_build.cuh"
+
+namespace cast {
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return -1;
+  if (dev < kMaxDevices) {
+    const int cached = g_sm_count[dev].load(std::memory_order_relaxed);
+    if (cached > 0) return cached;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return -1;
+  if (dev < kMaxDevices) g_sm_count[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+// Launch plan of the CUDA-core kernel: the key range of every sequence is cut
+// into `chunk`-key pieces until the grid covers the GPU about twice.
+struct SimtPlan {
+  int m_tiles, n_split, chunk, W;
+  size_t ws_bytes;
+};
+
+SimtPlan plan_simt(int B, int total_q, int H_q, int H_kv, int D, int max_pack, int max_kv, int sms) {
+  SimtPlan pl;
+  const int G = H_q / H_kv;
+  pl.m_tiles = (G * max_pack + simt::BM - 1) / simt::BM;
+  if (pl.m_tiles < 1) pl.m_tiles = 1;
+  pl.W = (max_pack + 63) / 64;
+  if (pl.W < 1) pl.W = 1;
+  const long long base = (long long)B * H_kv * pl.m_tiles;
+  const long long target = 2LL * (sms > 0 ? sms : 148);
+  const int kv = max_kv > 0 ? max_kv : 1;
+  int chunk = ((kv + simt::BN - 1) / simt::BN) * simt::BN;
+  int n_split = 1;
+  while (base * n_split < target && chunk > 4 * simt::BN) {
+    n_split *= 2;
+    chunk = (((kv + n_split - 1) / n_split + simt::BN - 1) / simt::BN) * simt::BN;
+  }
+  n_split = (kv + chunk - 1) / chunk;
+  pl.n_split = n_split;
+  pl.chunk = chunk;
+  pl.ws_bytes = n_split > 1 ? (size_t)n_split * total_q * H_q * (D + 2) * sizeof(float) : 0;
+  return pl;
+}
+
+template <typename T>
+int launch_simt(AttnParams& p, const SimtPlan& pl, cudaStream_t st) {
+  p.n_split = pl.n_split;
+  p.chunk = pl.chunk;
+  p.m_tiles = pl.m_tiles;
+  p.W = pl.W;
+  dim3 grid(pl.m_tiles, p.B * p.H_kv, pl.n_split);
+  if (p.D == 128) {
+    const size_t smem = simt::smem_bytes<128>(pl.W);
+    cudaFuncSetAttribute(attn_simt_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attn_simt_kernel<T, 128><<<grid, simt::NT, smem, st>>>(p);
+  } else {
+    const size_t smem = simt::smem_bytes<64>(pl.W);
+    cudaFuncSetAttribute(attn_simt_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attn_simt_kernel<T, 64><<<grid, simt::NT, smem, st>>>(p);
+  }
+  if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  if (pl.n_split > 1) {
+    const long long warps = (long long)p.total_q * p.H_q;
+    const int blocks = (int)((warps * 32 + 255) / 256);
+    attn_combine_kernel<T><<<blocks, 256, 0, st>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  }
+  return CAST_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+}  // namespace cast
+
+using namespace cast;
+
+extern "C" {
+
+const char* cast_strerror(int status) {
+  switch (status) {
+    case CAST_OK: return "ok";
+    case CAST_ERR_NULL: return "a required pointer is NULL";
+    case CAST_ERR_SHAPE: return "invalid shape (non-positive size, or H_q not a multiple of H_kv)";
+    case CAST_ERR_DTYPE: return "unsupported dtype (expected float32, bfloat16 or float16)";
+    case CAST_ERR_HEAD_DIM: return "unsupported head dim (expected 64 or 128)";
+    case CAST_ERR_PACK: return "pack too large (max_pack above CAST_MAX_PACK) or too few ancestor words per row";
+    case CAST_ERR_WORKSPACE: return "workspace smaller than cast_tree_attn_workspace_size()";
+    case CAST_ERR_ALIGN: return "misaligned pointer or stride (base 16-byte aligned, row/head strides multiples of 4 elements, dim stride 1)";
+    case CAST_ERR_TOPK: return "k out of range (1 <= k <= CAST_MAX_TOPK, k <= V) or L out of range";
+    case CAST_ERR_LAUNCH: return "CUDA launch failed";
+    case CAST_ERR_DEVICE: return "no usable CUDA device";
+    case CAST_ERR_MASK_MODE: return "pass exactly one of anc_words and parent";
+    case CAST_DEV_BAD_LAYOUT: return "device: cu_q/cu_kv/prefix_len/pack_len out of range or above max_pack/max_kv";
+    case CAST_DEV_BAD_PARENT: return "device: parent array is not a forest in pack order (need -1 <= parent[i] < i, parent[0] = -1)";
+    case CAST_DEV_TOPK_TIE: return "device: equal log-probs straddle the k-th place beyond the candidate margin";
+    case CAST_DEV_TIMEOUT: return "device: a bounded wait gave up";
+    case CAST_DEV_TREE_OVERFLOW: return "device: budget above max_budget";
+    default: return "unknown status";
+  }
+}
+
+int cast_version(void) { return 100; }
+
+int cast_device_error(cast_stream_t stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  const int zero = 0;
+  if (cudaMemcpyFromSymbolAsync(&h, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return CAST_ERR_LAUNCH;
+  if (cudaMemcpyToSymbolAsync(g_dev_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return CAST_ERR_LAUNCH;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return CAST_ERR_LAUNCH;
+  return h;
+}
+
+size_t cast_tree_attn_workspace_size(int dtype, int B, int total_q, int H_q, int H_kv, int D,
+                                     int max_pack, int max_kv) {
+  (void)dtype;
+  if (B <= 0 || total_q <= 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0) return 0;
+  const SimtPlan pl = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sm_count());
+  return pl.ws_bytes;
+}
+
+int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, int dtype,
+                       const int64_t* strides,
+                       const int32_t* cu_q, const int32_t* cu_kv,
+                       const int32_t* prefix_len, const int32_t* pack_len,
+                       const int64_t* anc_words, int anc_words_per_row,
+                       const int32_t* parent,
+                       int B, int total_q, int total_kv, int H_q, int H_kv, int D,
+                       float sm_scale, int max_pack, int max_kv,
+                       void* workspace, size_t workspace_bytes, cast_stream_t stream) {
+  if (dtype != CAST_F32 && dtype != CAST_BF16 && dtype != CAST_F16) return CAST_ERR_DTYPE;
+  if (B < 0 || total_q < 0 || total_kv < 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0 || max_pack < 0 ||
+      max_kv < 0)
+    return CAST_ERR_SHAPE;
+  if (D != 64 && D != 128) return CAST_ERR_HEAD_DIM;
+  if (max_pack > CAST_MAX_PACK) return CAST_ERR_PACK;
+  if (B == 0 || total_q == 0 || max_pack == 0) return CAST_OK;  // nothing to compute
+  if (!q || !k || !v || !out || !strides || !cu_q || !cu_kv || !prefix_len || !pack_len) return CAST_ERR_NULL;
+  if ((anc_words == nullptr) == (parent == nullptr)) return CAST_ERR_MASK_MODE;
+  if (anc_words && anc_words_per_row < 1) return CAST_ERR_PACK;
+  for (int t = 0; t < 4; ++t) {
+    if (strides[3 * t + 2] != 1) return CAST_ERR_ALIGN;
+    if (strides[3 * t + 0] % 4 != 0 || strides[3 * t + 1] % 4 != 0) return CAST_ERR_ALIGN;
+  }
+  const size_t ab = 16;
+  if (!aligned(q, ab) || !aligned(k, ab) || !aligned(v, ab) || !aligned(out, ab)) return CAST_ERR_ALIGN;
+  const int sms = sm_count();
+  if (sms <= 0) return CAST_ERR_DEVICE;
+
+  AttnParams p{};
+  p.q = q; p.k = k; p.v = v; p.out = out;
+  p.sq_m = strides[0]; p.sq_h = strides[1];
+  p.sk_m = strides[3]; p.sk_h = strides[4];
+  p.sv_m = strides[6]; p.sv_h = strides[7];
+  p.so_m = strides[9]; p.so_h = strides[10];
+  p.cu_q = cu_q; p.cu_kv = cu_kv; p.prefix_len = prefix_len; p.pack_len = pack_len;
+  p.anc_words = anc_words; p.anc_wpr = anc_words_per_row; p.parent = parent;
+  p.B = B; p.total_q = total_q; p.total_kv = total_kv; p.H_q = H_q; p.H_kv = H_kv; p.G = H_q / H_kv; p.D = D;
+  const float scale = sm_scale > 0.f ? sm_scale : 1.0f / sqrtf((float)D);
+  p.scale_log2 = scale * kLog2e;
+  p.max_pack = max_pack; p.max_kv = max_kv;
+
+  const SimtPlan pl = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sms);
+  if (pl.ws_bytes > 0) {
+    if (!workspace || workspace_bytes < pl.ws_bytes || !aligned(workspace, 16)) return CAST_ERR_WORKSPACE;
+    p.ws_o = static_cast<float*>(workspace);
+    p.ws_ml = p.ws_o + (size_t)pl.n_split * total_q * H_q * D;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case CAST_F32: return launch_simt<float>(p, pl, st);
+    case CAST_BF16: return launch_simt<__nv_bfloat16>(p, pl, st);
+    default: return launch_simt<__half>(p, pl, st);
+  }
+}
+
+int cast_block_topk(const double* logits, int64_t n_rows, int64_t V, int64_t row_stride, int k,
+                    int64_t* top_idx, double* top_lp, cast_stream_t stream) {
+  if (!logits || !top_idx || !top_lp) return CAST_ERR_NULL;
+  if (n_rows < 0 || V <= 0 || row_stride < V || V > 0x7fffffffLL || n_rows > 0x7fffffffLL) return CAST_ERR_SHAPE;
+  if (k < 1 || k > CAST_MAX_TOPK || k > V) return CAST_ERR_TOPK;
+  if (n_rows == 0) return CAST_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool vec = aligned(logits, 16) && (row_stride % 2 == 0);
+  const dim3 grid((unsigned)n_rows);
+  if (k <= 8) {
+    if (vec) block_topk_kernel<16, true><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);
+    else block_topk_kernel<16, false><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);
+  } else {
+    if (vec) block_topk_kernel<32, true><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);
+    else block_topk_kernel<32, false><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);
+  }
+  return cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
+}
+
+int cast_build_tree(const int64_t* top_idx, const double* top_lp, int B, int L, int k_cols, int k,
+                    const int32_t* budget, int max_budget,
+                    int32_t* token, int32_t* depth, int32_t* parent, double* score, int32_t* count,
+                    const int32_t* cu_q, int32_t* pack_parent,
+                    const int32_t* root_token, int32_t* pack_token,
+                    const int32_t* seq_len, int32_t* pack_pos,
+                    cast_stream_t stream) {
+  if (!top_idx || !top_lp || !budget || !token || !depth || !parent || !score || !count) return CAST_ERR_NULL;
+  if (B < 0 || L < 1 || L > CAST_MAX_DEPTH || k_cols < 1 || max_budget < 0 || max_budget >= CAST_MAX_PACK)
+    return CAST_ERR_SHAPE;
+  if (k < 1) return CAST_ERR_TOPK;
+  if (k > k_cols) k = k_cols;
+  if (k > CAST_MAX_TOPK) return CAST_ERR_TOPK;
+  if ((pack_token && !root_token) || (pack_pos && !seq_len)) return CAST_ERR_NULL;
+  if (!cu_q && (pack_parent || pack_token || pack_pos)) return CAST_ERR_NULL;
+  if (B == 0) return CAST_OK;
+  TreeArgs a{top_idx, top_lp, B, L, k_cols, k, budget, max_budget, token, depth, parent, score, count,
+             cu_q, pack_parent, root_token, pack_token, seq_len, pack_pos};
+  const size_t smem = tree_smem_bytes(max_budget > 0 ? max_budget : 1, L, k);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(build_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  build_tree_kernel<<<B, 32, smem, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
+}
+
+}  // extern "C"

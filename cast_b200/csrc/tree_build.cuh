@@ -1,0 +1,401 @@
+// Tree construction on the GPU: per-row top-k of fp64 log-softmax, then the
+// best-first tree of each sequence, node for node the reference's pop order.
+#pragma once
+
+#include "common.cuh"
+
+namespace cast {
+
+// ---------------------------------------------------------------------------
+// block_topk (cast_trees/tree.py:20-26).
+//
+// One CTA per row of V logits, one pass over HBM. Each thread keeps
+//  * an online (running max m_t, sum_t of exp(x - m_t)) pair, and
+//  * its KC best (x, index) candidates, sorted by x descending; because a thread
+//    visits its elements in increasing index order, an equal x never displaces
+//    an earlier one, which is the stable sort's lower-index-first rule.
+// The CTA merges both, forms lp = (x - M) - log(sum exp(x - M)) with the
+// reference's operation order, and re-sorts the KC best by (lp desc, index
+// asc): the subtraction can make distinct x equal in lp, and the reference
+// sorts on lp. Any element outside the KC candidates has lp <= the KC-th one;
+// it could only enter the top k if the k-th and KC-th lp were equal, which is
+// reported as CAST_DEV_TOPK_TIE instead of returning a possibly different order.
+// ---------------------------------------------------------------------------
+namespace topk {
+constexpr int NT = 256;
+constexpr int NW = NT / 32;
+}
+
+template <int KC>
+struct CandList {
+  double x[KC];
+  int idx[KC];  // -1 = empty slot (ranks below every real element)
+
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int i = 0; i < KC; ++i) { x[i] = -INFINITY; idx[i] = -1; }
+  }
+  // j is larger than every index already held (increasing visit order).
+  __device__ __forceinline__ void offer(double v, int j) {
+    if (idx[KC - 1] >= 0 && !(v > x[KC - 1])) return;
+    x[KC - 1] = v;
+    idx[KC - 1] = j;
+#pragma unroll
+    for (int i = KC - 1; i > 0; --i) {
+      const bool up = idx[i - 1] < 0 || x[i] > x[i - 1];
+      if (up) {
+        const double tx = x[i]; x[i] = x[i - 1]; x[i - 1] = tx;
+        const int ti = idx[i]; idx[i] = idx[i - 1]; idx[i - 1] = ti;
+      }
+    }
+  }
+  __device__ __forceinline__ void pop_front() {
+#pragma unroll
+    for (int i = 0; i < KC - 1; ++i) { x[i] = x[i + 1]; idx[i] = idx[i + 1]; }
+    x[KC - 1] = -INFINITY;
+    idx[KC - 1] = -1;
+  }
+};
+
+// (a_x, a_i) ranks before (b_x, b_i): larger x, then smaller index; empty last.
+__device__ __forceinline__ bool cand_before(double ax, int ai, double bx, int bi) {
+  if (ai < 0) return false;
+  if (bi < 0) return true;
+  return ax > bx || (ax == bx && ai < bi);
+}
+
+__device__ __forceinline__ void online_add(double& m, double& s, double v) {
+  if (v == -INFINITY) return;
+  if (v > m) {
+    s = s * exp(m - v) + 1.0;
+    m = v;
+  } else {
+    s += exp(v - m);
+  }
+}
+
+template <int KC, bool VEC2>
+__global__ void __launch_bounds__(topk::NT)
+block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
+                  int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
+  using namespace topk;
+  __shared__ double s_m[NW], s_s[NW];
+  __shared__ double s_cx[NW * KC];
+  __shared__ int s_ci[NW * KC];
+  __shared__ double s_fx[KC], s_flp[KC];
+  __shared__ int s_fi[KC];
+
+  const int64_t row = blockIdx.x;
+  const double* x = logits + row * row_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  CandList<KC> cl;
+  cl.init();
+  double m = -INFINITY, s = 0.0;
+  if (VEC2) {
+    const double2* x2 = reinterpret_cast<const double2*>(x);
+    const int64_t n2 = V >> 1;
+    int64_t i = tid;
+    for (; i + 3 * NT < n2; i += 4 * NT) {
+      double2 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcs(x2 + i + u * NT);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = (int)(2 * (i + u * NT));
+        online_add(m, s, v[u].x); cl.offer(v[u].x, j);
+        online_add(m, s, v[u].y); cl.offer(v[u].y, j + 1);
+      }
+    }
+    for (; i < n2; i += NT) {
+      const double2 v = __ldcs(x2 + i);
+      const int j = (int)(2 * i);
+      online_add(m, s, v.x); cl.offer(v.x, j);
+      online_add(m, s, v.y); cl.offer(v.y, j + 1);
+    }
+    if ((V & 1) && tid == 0) {
+      const double v = x[V - 1];
+      online_add(m, s, v); cl.offer(v, (int)(V - 1));
+    }
+  } else {
+    for (int64_t i = tid; i < V; i += NT) {
+      const double v = x[i];
+      online_add(m, s, v); cl.offer(v, (int)i);
+    }
+  }
+
+  // (m, s) reduction: warp, then CTA
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const double om = __shfl_xor_sync(0xffffffffu, m, off);
+    const double os = __shfl_xor_sync(0xffffffffu, s, off);
+    const double mm = fmax(m, om);
+    if (mm != -INFINITY) {
+      s = (m == -INFINITY ? 0.0 : s * exp(m - mm)) + (om == -INFINITY ? 0.0 : os * exp(om - mm));
+    }
+    m = mm;
+  }
+  if (lane == 0) { s_m[warp] = m; s_s[warp] = s; }
+
+  // candidate tournament inside each warp: KC rounds of a warp arg-best
+  for (int rnd = 0; rnd < KC; ++rnd) {
+    double bx = cl.x[0];
+    int bi = cl.idx[0];
+    int bl = lane;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const double ox = __shfl_xor_sync(0xffffffffu, bx, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      const int ol = __shfl_xor_sync(0xffffffffu, bl, off);
+      if (cand_before(ox, oi, bx, bi) || (oi == bi && ol < bl)) { bx = ox; bi = oi; bl = ol; }
+    }
+    if (lane == bl && bi >= 0) cl.pop_front();
+    if (lane == 0) { s_cx[warp * KC + rnd] = bx; s_ci[warp * KC + rnd] = bi; }
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    double M = s_m[0];
+    for (int w = 1; w < NW; ++w) M = fmax(M, s_m[w]);
+    double S = 0.0;
+    for (int w = 0; w < NW; ++w)
+      if (s_m[w] != -INFINITY) S += s_s[w] * exp(s_m[w] - M);
+    const double lse = log(S);
+
+    // merge the NW sorted warp lists (KC rounds, each lane scans NW*KC/32 slots)
+    for (int rnd = 0; rnd < KC; ++rnd) {
+      double bx = -INFINITY;
+      int bi = -1, bslot = -1;
+      for (int c = lane; c < NW * KC; c += 32) {
+        if (cand_before(s_ci[c] >= 0 ? s_cx[c] : -INFINITY, s_ci[c], bx, bi)) {
+          bx = s_cx[c]; bi = s_ci[c]; bslot = c;
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const double ox = __shfl_xor_sync(0xffffffffu, bx, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        const int os = __shfl_xor_sync(0xffffffffu, bslot, off);
+        if (cand_before(ox, oi, bx, bi)) { bx = ox; bi = oi; bslot = os; }
+      }
+      if (lane == 0) {
+        s_fx[rnd] = bx;
+        s_fi[rnd] = bi;
+        if (bslot >= 0) s_ci[bslot] = -1;  // taken
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      int n = 0;
+      for (int c = 0; c < KC; ++c) {
+        if (s_fi[c] < 0) break;
+        s_flp[c] = (s_fx[c] - M) - lse;
+        ++n;
+      }
+      // stable insertion sort by (lp desc, index asc)
+      for (int a = 1; a < n; ++a) {
+        const double lv = s_flp[a];
+        const int iv = s_fi[a];
+        int c = a - 1;
+        while (c >= 0 && (s_flp[c] < lv || (s_flp[c] == lv && s_fi[c] > iv))) {
+          s_flp[c + 1] = s_flp[c];
+          s_fi[c + 1] = s_fi[c];
+          --c;
+        }
+        s_flp[c + 1] = lv;
+        s_fi[c + 1] = iv;
+      }
+      if (V > KC && n == KC && s_flp[k - 1] == s_flp[KC - 1]) report(CAST_DEV_TOPK_TIE);
+      for (int c = 0; c < k; ++c) {
+        top_idx[row * k + c] = c < n ? (int64_t)s_fi[c] : (int64_t)0;
+        top_lp[row * k + c] = c < n ? s_flp[c] : -INFINITY;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// build_tree (cast_trees/tree.py:29-49), one warp per tree.
+//
+// The reference pops a heap keyed by (neg, depth, parent, rank) and pushes all
+// k children of every popped node. Siblings share depth and parent, so a
+// node's children leave that heap in the order of (neg_child, rank). Keeping
+// only each expanded node's next unpopped child in the candidate set therefore
+// never changes the minimum: any pushed-but-unpopped child has a sibling of
+// equal or smaller key in the set. The set holds at most budget + 1 entries;
+// each pop is a warp arg-min over it, the popped slot takes the next sibling,
+// and the new node's first child is appended. Keys compare exactly like
+// Python tuples: neg as an ordered 64-bit pattern (with -0.0 folded into
+// +0.0, which Python treats as equal), then (depth, parent + 1, rank) packed
+// into a second word. Scores use the reference's float64 operations:
+// -lp[0, r] at depth 1, neg_parent - lp[d, r] below.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t ordered_key(double v) {
+  const uint64_t u = (uint64_t)__double_as_longlong(v + 0.0);
+  return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
+}
+
+struct TreeArgs {
+  const int64_t* top_idx;
+  const double* top_lp;
+  int B, L, k_cols, k;
+  const int32_t* budget;
+  int max_budget;
+  int32_t* token;
+  int32_t* depth;
+  int32_t* parent;
+  double* score;
+  int32_t* count;
+  const int32_t* cu_q;
+  int32_t* pack_parent;
+  const int32_t* root_token;
+  int32_t* pack_token;
+  const int32_t* seq_len;
+  int32_t* pack_pos;
+};
+
+__host__ __device__ inline size_t tree_smem_bytes(int max_budget, int L, int k) {
+  const size_t nc = (size_t)max_budget + 1;
+  return nc * (2 * sizeof(uint64_t) + sizeof(double) + 4 * sizeof(int)) +  // candidates
+         (size_t)max_budget * sizeof(double) +                            // node neg
+         ((size_t)max_budget + 1) * k * sizeof(unsigned char) +            // child order per node (+root)
+         (size_t)L * k * sizeof(double) + 64;                              // lp rows
+}
+
+__global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x;
+  const int k = a.k, L = a.L;
+  const int nc_max = a.max_budget + 1;
+  uint64_t* c_hi = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* c_lo = c_hi + nc_max;
+  double* c_neg = reinterpret_cast<double*>(c_lo + nc_max);
+  int* c_par = reinterpret_cast<int*>(c_neg + nc_max);  // parent node (-1 = root)
+  int* c_j = c_par + nc_max;                            // position in the parent's child order
+  int* c_d = c_j + nc_max;                              // depth of the candidate
+  int* c_r = c_d + nc_max;                              // rank
+  double* n_neg = reinterpret_cast<double*>(c_r + nc_max);
+  double* s_lp = n_neg + a.max_budget;
+  unsigned char* order = reinterpret_cast<unsigned char*>(s_lp + (size_t)L * k);  // [(1 + max_budget)][k], row 0 = root
+
+  int budget = a.budget[b];
+  if (budget > a.max_budget || budget < 0) {
+    if (lane == 0) { report(CAST_DEV_TREE_OVERFLOW); a.count[b] = 0; }
+    return;
+  }
+  const double* lp_g = a.top_lp + (size_t)b * L * a.k_cols;
+  const int64_t* idx_g = a.top_idx + (size_t)b * L * a.k_cols;
+  for (int e = lane; e < L * k; e += 32) s_lp[e] = lp_g[(e / k) * a.k_cols + (e % k)];
+  __syncwarp();
+
+  // child order of a node whose own neg is `base` (root: children neg = -lp[0, r])
+  auto child_order = [&](int slot, bool root, double base, int d) {
+    uint64_t hi = ~0ull;
+    if (lane < k) hi = ordered_key(root ? -s_lp[lane] : base - s_lp[d * k + lane]);
+    int rank = 0;
+    for (int r2 = 0; r2 < k; ++r2) {
+      const uint64_t h2 = __shfl_sync(0xffffffffu, hi, r2);
+      if (lane < k && (h2 < hi || (h2 == hi && r2 < lane))) ++rank;
+    }
+    if (lane < k) order[(size_t)slot * k + rank] = (unsigned char)lane;
+    __syncwarp();
+  };
+
+  int ncand = 0;
+  if (budget > 0 && k > 0 && L > 0) {
+    child_order(0, true, 0.0, 0);
+    if (lane == 0) {
+      const int r = order[0];
+      const double neg = -s_lp[r];
+      c_hi[0] = ordered_key(neg);
+      c_lo[0] = (1ull << 40) | (0ull << 8) | (uint64_t)r;
+      c_neg[0] = neg; c_par[0] = -1; c_j[0] = 0; c_d[0] = 1; c_r[0] = r;
+    }
+    ncand = 1;
+    __syncwarp();
+  }
+
+  int n = 0;
+  const int q0 = a.cu_q ? a.cu_q[b] : 0;
+  bool pack_ok = true;
+  if (a.cu_q && lane == 0) {
+    pack_ok = q0 >= 0 && (long long)q0 + 1 + budget <= (long long)a.cu_q[b + 1];
+    if (!pack_ok) report(CAST_DEV_BAD_LAYOUT);
+  }
+  pack_ok = __shfl_sync(0xffffffffu, pack_ok ? 1 : 0, 0) != 0;
+
+  while (n < budget && ncand > 0) {
+    // arg-min over the candidate set
+    uint64_t bh = ~0ull, bl = ~0ull;
+    int bs = -1;
+    for (int c = lane; c < ncand; c += 32) {
+      const uint64_t h = c_hi[c], l = c_lo[c];
+      if (bs < 0 || h < bh || (h == bh && l < bl)) { bh = h; bl = l; bs = c; }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const uint64_t oh = __shfl_xor_sync(0xffffffffu, bh, off);
+      const uint64_t ol = __shfl_xor_sync(0xffffffffu, bl, off);
+      const int os = __shfl_xor_sync(0xffffffffu, bs, off);
+      if (os >= 0 && (bs < 0 || oh < bh || (oh == bh && ol < bl))) { bh = oh; bl = ol; bs = os; }
+    }
+    const int slot = bs;
+    const double neg = c_neg[slot];
+    const int par = c_par[slot], j = c_j[slot], d = c_d[slot], r = c_r[slot];
+    const int me = n;
+    __syncwarp();  // every lane has read the slot before lane 0 rewrites it
+    if (lane == 0) {
+      const int tok = (int)idx_g[(size_t)(d - 1) * a.k_cols + r];
+      const size_t o = (size_t)b * a.max_budget + me;
+      a.token[o] = tok;
+      a.depth[o] = d;
+      a.parent[o] = par;
+      a.score[o] = -neg;
+      n_neg[me] = neg;
+      if (a.cu_q && pack_ok) {
+        if (a.pack_parent) a.pack_parent[q0 + 1 + me] = par + 1;
+        if (a.pack_token) a.pack_token[q0 + 1 + me] = tok;
+        if (a.pack_pos) a.pack_pos[q0 + 1 + me] = a.seq_len[b] + d;
+      }
+      // the popped slot takes the next sibling, or the last candidate
+      if (j + 1 < k) {
+        const int r2 = order[(size_t)(par + 1) * k + j + 1];
+        const double sneg = (par < 0) ? -s_lp[r2] : n_neg[par] - s_lp[(size_t)(d - 1) * k + r2];
+        c_hi[slot] = ordered_key(sneg);
+        c_lo[slot] = ((uint64_t)d << 40) | ((uint64_t)(par + 1) << 8) | (uint64_t)r2;
+        c_neg[slot] = sneg; c_j[slot] = j + 1; c_r[slot] = r2;
+      } else {
+        const int last = ncand - 1;
+        c_hi[slot] = c_hi[last]; c_lo[slot] = c_lo[last]; c_neg[slot] = c_neg[last];
+        c_par[slot] = c_par[last]; c_j[slot] = c_j[last]; c_d[slot] = c_d[last]; c_r[slot] = c_r[last];
+      }
+    }
+    if (j + 1 >= k) --ncand;
+    __syncwarp();
+    if (d < L) {
+      child_order(me + 1, false, neg, d);
+      if (lane == 0) {
+        const int r2 = order[(size_t)(me + 1) * k];
+        const double cneg = neg - s_lp[(size_t)d * k + r2];
+        const int c = ncand;
+        c_hi[c] = ordered_key(cneg);
+        c_lo[c] = ((uint64_t)(d + 1) << 40) | ((uint64_t)(me + 1) << 8) | (uint64_t)r2;
+        c_neg[c] = cneg; c_par[c] = me; c_j[c] = 0; c_d[c] = d + 1; c_r[c] = r2;
+      }
+      ++ncand;
+    }
+    ++n;
+    __syncwarp();
+  }
+  if (lane == 0) {
+    a.count[b] = n;
+    if (a.cu_q && pack_ok) {
+      if (a.pack_parent) a.pack_parent[q0] = -1;
+      if (a.pack_token) a.pack_token[q0] = a.root_token[b];
+      if (a.pack_pos) a.pack_pos[q0] = a.seq_len[b];
+    }
+  }
+}
+
+}  // namespace cast

@@ -1,0 +1,98 @@
+"""Ragged ancestor-masked tree-verification attention on B200 (drop-in).
+
+``varlen_tree_attention`` keeps the call signature, argument meaning and
+output of cast_trees/tree_attn.py:116-139 and runs the sm_100a kernels of
+``libcast_b200.so`` through its C ABI (include/cast_b200.h). Two extensions,
+both keyword-only and optional:
+
+* ``parent=``: int32 [total_q] pack-local parents (-1 for the root,
+  parent[i] < i, the convention of cast_trees/serving.py:217-222). The kernel
+  builds each token's ancestor bitset in shared memory, so packs are not
+  limited to 64 tokens; pass ``ancestor_mask=None`` with it.
+  ``ancestor_mask`` may also be int64 [total_q, W] (W words per token).
+* ``max_pack=`` / ``max_kv=``: host-side bounds of pack_len and
+  prefix_len + pack_len. Given, the call needs no device-to-host read; omitted,
+  they are read back once, as the reference reads cu_q back (tree_attn.py:128).
+"""
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.CAST_F32, torch.bfloat16: _lib.CAST_BF16, torch.float16: _lib.CAST_F16}
+
+
+def _kernel_ready(t):
+    """dim stride 1, row/head strides multiples of 4 elements, 16-byte aligned base."""
+    s = t.stride()
+    return s[2] == 1 and s[0] % 4 == 0 and s[1] % 4 == 0 and t.data_ptr() % 16 == 0
+
+
+def _prep(t):
+    return t if _kernel_ready(t) else t.contiguous()
+
+
+def _i32(t, device):
+    t = torch.as_tensor(t, device=device)
+    return t if (t.dtype == torch.int32 and t.is_contiguous()) else t.to(torch.int32).contiguous()
+
+
+def workspace_size(dtype, B, total_q, H_q, H_kv, D, max_pack, max_kv):
+    return int(_lib.lib().cast_tree_attn_workspace_size(_DTYPES[dtype], B, total_q, H_q, H_kv, D,
+                                                        max_pack, max_kv))
+
+
+def varlen_tree_attention(q, k, v, cu_q, cu_kv, prefix_len, pack_len, ancestor_mask=None, sm_scale=None,
+                          *, parent=None, max_pack=None, max_kv=None, out=None, workspace=None):
+    """q: [total_q, H_q, D], k/v: [total_kv, H_kv, D] -> [total_q, H_q, D] (q's dtype).
+
+    cu_q / cu_kv: int32 [B+1] offsets of packs and of concat(prefix, pack).
+    prefix_len / pack_len: int32 [B]. ancestor_mask: int64 [total_q] (or
+    [total_q, W]); or pass parent= instead. Rows that see no key give 0.
+    """
+    total_q, H_q, D = q.shape
+    total_kv, H_kv = k.shape[0], k.shape[1]
+    assert H_q % H_kv == 0
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if not q.is_cuda:
+        raise RuntimeError("cast_b200.varlen_tree_attention needs CUDA tensors (no CPU path)")
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError(f"q/k/v must share one of {list(_DTYPES)}; got {q.dtype}, {k.dtype}, {v.dtype}")
+    if (ancestor_mask is None) == (parent is None):
+        raise ValueError("pass exactly one of ancestor_mask and parent")
+    dev = q.device
+    B = int(pack_len.shape[0])
+    q, k, v = _prep(q), _prep(k), _prep(v)
+    if out is None:
+        out = torch.empty_like(q)
+    if not _kernel_ready(out):
+        raise ValueError("out must have dim stride 1, row/head strides multiple of 4 and a 16-byte aligned base")
+    cu_q_t, cu_kv_t = _i32(cu_q, dev), _i32(cu_kv, dev)
+    prefix_t, pack_t = _i32(prefix_len, dev), _i32(pack_len, dev)
+    if max_pack is None:
+        max_pack = int(pack_t.max().item()) if B > 0 else 0
+    if max_kv is None:
+        max_kv = int((prefix_t + pack_t).max().item()) if B > 0 else 0
+    anc_ptr, wpr, par_ptr = None, 0, None
+    if ancestor_mask is not None:
+        anc = torch.as_tensor(ancestor_mask, device=dev)
+        anc = anc.to(torch.int64).reshape(total_q, -1).contiguous()
+        anc_ptr, wpr = anc.data_ptr(), int(anc.shape[1])
+    else:
+        par = _i32(parent, dev)
+        par_ptr = par.data_ptr()
+    ws_bytes = workspace_size(q.dtype, B, total_q, H_q, H_kv, D, max_pack, max_kv)
+    if ws_bytes > 0 and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes):
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    strides = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride(), *out.stride())
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    code = _lib.lib().cast_tree_attn_fwd(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), _DTYPES[q.dtype], ctypes.addressof(strides),
+        cu_q_t.data_ptr(), cu_kv_t.data_ptr(), prefix_t.data_ptr(), pack_t.data_ptr(),
+        anc_ptr, wpr, par_ptr, B, total_q, total_kv, H_q, H_kv, D, float(sm_scale), int(max_pack), int(max_kv),
+        workspace.data_ptr() if ws_bytes > 0 else None, ws_bytes, stream)
+    _lib.check(code, "cast_tree_attn_fwd")
+    return out

@@ -1,0 +1,156 @@
+/*
+ * cast_b200: C ABI of the B200 (sm_100a) ragged tree-verification path.
+ *
+ * Replaces, behind a plain C interface (device pointers, sizes, a stream):
+ *   - cast_trees/tree_attn.py:116-139  varlen_tree_attention (host wrapper)
+ *   - cast_trees/tree_attn.py:17-92    _tree_attn_fwd (the Triton kernel)
+ *   - cast_trees/tree_attn.py:104-113  _tile_schedule (host tile list + D2H sync)
+ *   - cast_trees/tree.py:20-26         block_topk
+ *   - cast_trees/tree.py:29-49         build_tree
+ *   - cast_trees/serving.py:213-222    packed tok/pos/ancestor layout of one verify pass
+ *
+ * Conventions shared by every entry point:
+ *   - All array arguments are DEVICE pointers owned by the caller. The library
+ *     allocates nothing per call; scratch space is passed in as `workspace`.
+ *   - Work is enqueued on `stream` (a cudaStream_t / CUstream; NULL = the legacy
+ *     default stream) and is asynchronous: a return of CAST_OK means the
+ *     launch was accepted.
+ *   - Negative return codes are argument errors found on the host before any
+ *     launch. Kernels that find inconsistent device-side metadata skip the bad
+ *     unit and record a positive code in a per-device error word; read (and
+ *     clear) it with cast_device_error(), which synchronises the stream.
+ *   - No entry point aborts, traps or prints.
+ *   - Entry points are re-entrant; concurrent calls on different streams must
+ *     use different workspaces.
+ */
+#ifndef CAST_B200_H
+#define CAST_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* cast_stream_t;  /* cudaStream_t */
+
+/* element types of q / k / v / out */
+enum cast_dtype { CAST_F32 = 0, CAST_BF16 = 1, CAST_F16 = 2 };
+
+enum cast_status {
+  CAST_OK = 0,
+  CAST_ERR_NULL = -1,         /* a required pointer is NULL */
+  CAST_ERR_SHAPE = -2,        /* non-positive size, or H_q % H_kv != 0 */
+  CAST_ERR_DTYPE = -3,        /* unknown dtype */
+  CAST_ERR_HEAD_DIM = -4,     /* head dim not in {64, 128} */
+  CAST_ERR_PACK = -5,         /* max_pack above CAST_MAX_PACK, or anc words too few */
+  CAST_ERR_WORKSPACE = -6,    /* workspace smaller than cast_tree_attn_workspace_size() */
+  CAST_ERR_ALIGN = -7,        /* a pointer or stride breaks the kernel's alignment rule */
+  CAST_ERR_TOPK = -8,         /* k out of range [1, CAST_MAX_TOPK] or V < k */
+  CAST_ERR_LAUNCH = -9,       /* the CUDA launch itself failed */
+  CAST_ERR_DEVICE = -10,      /* no usable CUDA device */
+  CAST_ERR_MASK_MODE = -11,   /* both or neither of anc_words / parent given */
+  /* device-side codes (positive), reported by cast_device_error() */
+  CAST_DEV_BAD_LAYOUT = 1,    /* cu/prefix/pack arrays out of range or above max_pack/max_kv */
+  CAST_DEV_BAD_PARENT = 2,    /* parent[i] >= i or < -1 (or parent[0] != -1) */
+  CAST_DEV_TOPK_TIE = 3,      /* more equal log-probs at the k-th place than the candidate margin */
+  CAST_DEV_TIMEOUT = 4,       /* a bounded wait inside a kernel gave up */
+  CAST_DEV_TREE_OVERFLOW = 5  /* build_tree budget above max_budget */
+};
+
+#define CAST_MAX_PACK 1024    /* largest pack (1 + N) the attention kernels accept */
+#define CAST_MAX_TOPK 24      /* largest k of block_topk / build_tree */
+#define CAST_MAX_DEPTH 64     /* largest L of build_tree */
+
+/* Human-readable text for a status code (never NULL). */
+const char* cast_strerror(int status);
+
+/* Library ABI version: 100 * major + minor. */
+int cast_version(void);
+
+/*
+ * Reads and clears the device error word of the current device after
+ * synchronising `stream`. Returns 0 (CAST_OK), a positive CAST_DEV_* code,
+ * or CAST_ERR_LAUNCH if the CUDA runtime itself reports an error.
+ */
+int cast_device_error(cast_stream_t stream);
+
+/*
+ * Ragged ancestor-masked GQA tree attention, forward.
+ * Replaces cast_trees/tree_attn.py:116 varlen_tree_attention and the kernel
+ * it launches (tree_attn.py:17-92).
+ *
+ * Sequence b owns the packed query rows [cu_q[b], cu_q[b] + pack_len[b]) and
+ * the key/value rows [cu_kv[b], cu_kv[b] + prefix_len[b] + pack_len[b]): its
+ * prefix first, then its pack (tree_attn.py:39-41,71). Query row i of the pack
+ * sees every prefix key and pack key j iff bit j of its ancestor bitset is set.
+ *
+ * q: [total_q, H_q, D], k/v: [total_kv, H_kv, D], out: [total_q, H_q, D]; all
+ *   of `dtype`; strides[12] = element strides (row, head, dim) of q, k, v, out.
+ *   The dim stride must be 1.
+ * anc_words: int64 [total_q, anc_words_per_row] ancestor bitsets (bit j of word
+ *   j/64), the reference's `ancestor_mask` when anc_words_per_row == 1; or NULL.
+ * parent: int32 [total_q] pack-local parents (-1 for the root, parent[i] < i),
+ *   from which the kernel builds the bitsets in shared memory; or NULL.
+ *   Exactly one of anc_words / parent is given.
+ * max_pack / max_kv: host-side upper bounds of pack_len[b] and
+ *   prefix_len[b] + pack_len[b]; they size the launch so no device-to-host
+ *   read is needed (the reference reads cu_q back every call, tree_attn.py:128).
+ * sm_scale: softmax scale; pass a value <= 0 for the default 1/sqrt(D)
+ *   (tree_attn.py:125-126).
+ * Rows that see no key are written as 0 (tree_attn.py:89).
+ */
+int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, int dtype,
+                       const int64_t* strides,
+                       const int32_t* cu_q, const int32_t* cu_kv,
+                       const int32_t* prefix_len, const int32_t* pack_len,
+                       const int64_t* anc_words, int anc_words_per_row,
+                       const int32_t* parent,
+                       int B, int total_q, int total_kv, int H_q, int H_kv, int D,
+                       float sm_scale, int max_pack, int max_kv,
+                       void* workspace, size_t workspace_bytes, cast_stream_t stream);
+
+/*
+ * Bytes of workspace cast_tree_attn_fwd needs for these sizes (0 is possible).
+ * Pure host arithmetic; the same arguments must be passed to the call.
+ */
+size_t cast_tree_attn_workspace_size(int dtype, int B, int total_q, int H_q, int H_kv, int D,
+                                     int max_pack, int max_kv);
+
+/*
+ * Per-row fp64 log-softmax and top-k, bit-compatible with
+ * cast_trees/tree.py:20-26 block_topk: ties keep the lower index first.
+ * logits: float64 [n_rows, V] with row stride `row_stride` (elements).
+ * top_idx: int64 [n_rows, k]; top_lp: float64 [n_rows, k], best first.
+ */
+int cast_block_topk(const double* logits, int64_t n_rows, int64_t V, int64_t row_stride, int k,
+                    int64_t* top_idx, double* top_lp, cast_stream_t stream);
+
+/*
+ * Best-first prefix-closed trees, node order identical to
+ * cast_trees/tree.py:29-49 build_tree (pop order of the heap keyed by
+ * (-path_logprob, depth, parent, rank)).
+ * top_idx / top_lp: [B, L, k_cols] (row-major), k = min(k, k_cols) is used.
+ * budget: int32 [B] non-root node count per tree (<= max_budget).
+ * Outputs [B, max_budget] (row b holds count[b] nodes): token (int32),
+ * depth (int32, 1..L), parent (int32, -1 = root) and score (float64).
+ * Optional pack layout of cast_trees/serving.py:213-222 (pass NULL to skip):
+ *   cu_q (int32 [B+1]) gives each pack's first row; then
+ *   pack_parent[cu_q[b] + 0] = -1, pack_parent[cu_q[b] + 1 + i] = parent_i + 1,
+ *   pack_token (needs root_token int32 [B]) = root, then node tokens,
+ *   pack_pos (needs seq_len int32 [B]) = seq_len, then seq_len + depth_i.
+ */
+int cast_build_tree(const int64_t* top_idx, const double* top_lp, int B, int L, int k_cols, int k,
+                    const int32_t* budget, int max_budget,
+                    int32_t* token, int32_t* depth, int32_t* parent, double* score, int32_t* count,
+                    const int32_t* cu_q, int32_t* pack_parent,
+                    const int32_t* root_token, int32_t* pack_token,
+                    const int32_t* seq_len, int32_t* pack_pos,
+                    cast_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAST_B200_H */

@@ -144,18 +144,20 @@ def attn_cfg1(tree, verify):
                         S=S, P=P)
 
 
-def ragged_scenario(seed=11, B=6, Hq=8, Hkv=2, D=64):
+def ragged_scenario(seed=11, B=6, Hq=8, Hkv=2, D=64, s_range=(0, 300), p_range=(1, 64)):
     """Seeded ragged batch built like tests/test_tree_attn.py:11-37, on the CPU.
 
     Draw order per request: prefix length, pack length, parents, then q, k, v.
-    Prefix lengths may be 0 and packs may hold a single token (edge cases).
+    With the defaults, prefix lengths may be 0 and packs may hold a single
+    token (edge cases); s_range=(200, 400), p_range=(2, 64) with B=8, Hq=32,
+    Hkv=8, D=128 is the reference test's own scenario.
     """
     g = torch.Generator().manual_seed(seed)
     qs, ks, vs, bits, reqs = [], [], [], [], []
     cu_q, cu_kv = [0], [0]
     for _ in range(B):
-        S = int(torch.randint(0, 300, (1,), generator=g))
-        P = int(torch.randint(1, 64, (1,), generator=g))
+        S = int(torch.randint(s_range[0], s_range[1], (1,), generator=g))
+        P = int(torch.randint(p_range[0], p_range[1], (1,), generator=g))
         parent = [-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, P)]
         qs.append(torch.randn(P, Hq, D, generator=g))
         ks.append(torch.randn(S + P, Hkv, D, generator=g))

@@ -1,0 +1,84 @@
+"""The C-ABI library without a GPU: it loads, exports every declared symbol,
+and rejects bad arguments on the host before touching the device."""
+import ctypes
+import re
+
+import pytest
+
+from cast_b200 import _lib
+
+
+@pytest.fixture(scope="module")
+def L():
+    return _lib.lib()
+
+
+def test_every_declared_symbol_is_exported(L):
+    decl = set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(cast_\w+)\s*\(", _lib.HEADER.read_text(), re.M))
+    assert decl == set(_lib.EXPORTS)
+    for name in decl:
+        assert hasattr(L, name), name
+
+
+def test_strerror_and_version(L):
+    assert L.cast_version() == 100
+    assert L.cast_strerror(0) == b"ok"
+    for code in list(range(-11, 0)) + list(range(1, 6)):
+        assert L.cast_strerror(code) != b"unknown status"
+    assert L.cast_strerror(12345) == b"unknown status"
+
+
+def _attn(L, **over):
+    args = dict(q=1 << 12, k=1 << 12, v=1 << 12, out=1 << 12, dtype=1, strides=None, cu_q=8, cu_kv=8,
+                prefix=8, pack=8, anc=None, wpr=0, parent=8, B=1, total_q=4, total_kv=8, H_q=8, H_kv=2,
+                D=128, scale=0.0, max_pack=4, max_kv=8, ws=None, ws_bytes=0, stream=None)
+    args.update(over)
+    strides = (ctypes.c_int64 * 12)(*([1024, 128, 1] * 4))
+    if args["strides"] is None:
+        args["strides"] = ctypes.addressof(strides)
+    return L.cast_tree_attn_fwd(*args.values())
+
+
+def test_attention_argument_checks(L):
+    # every one of these returns before any CUDA call
+    assert _attn(L, dtype=7) == -3
+    assert _attn(L, H_q=6, H_kv=4) == -2
+    assert _attn(L, D=96) == -4
+    assert _attn(L, max_pack=4096) == -5
+    assert _attn(L, q=None) == -1
+    assert _attn(L, parent=None) == -11           # neither mask form
+    assert _attn(L, anc=8, wpr=1) == -11          # both mask forms
+    assert _attn(L, parent=None, anc=8, wpr=0) == -5
+    bad = (ctypes.c_int64 * 12)(*([1024, 128, 2] + [1024, 128, 1] * 3))
+    assert _attn(L, strides=ctypes.addressof(bad)) == -7
+    assert _attn(L, q=(1 << 12) + 4) == -7
+    assert _attn(L, B=0) == 0                     # empty batch is a no-op
+    assert _attn(L, max_pack=0) == 0
+
+
+def test_workspace_size_is_host_arithmetic(L):
+    # small batch, long prefix: the key range is split and partials need scratch
+    big = L.cast_tree_attn_workspace_size(1, 2, 258, 32, 8, 128, 129, 32897)
+    assert big > 0 and big % 4 == 0
+    # many sequences: no split, no scratch
+    assert L.cast_tree_attn_workspace_size(1, 64, 8192, 32, 8, 128, 128, 8199) == 0
+    assert L.cast_tree_attn_workspace_size(1, 2, 258, 30, 8, 128, 129, 32897) == 0   # bad heads
+
+
+def test_tree_argument_checks(L):
+    p = 1 << 12
+    assert L.cast_block_topk(None, 1, 10, 10, 2, p, p, None) == -1
+    assert L.cast_block_topk(p, 1, 10, 10, 0, p, p, None) == -8
+    assert L.cast_block_topk(p, 1, 10, 10, 11, p, p, None) == -8
+    assert L.cast_block_topk(p, 1, 10, 10, 25, p, p, None) == -8
+    assert L.cast_block_topk(p, 1, 10, 5, 2, p, p, None) == -2        # row stride < V
+    assert L.cast_block_topk(p, 0, 10, 10, 2, p, p, None) == 0         # no rows
+    nul = None
+    assert L.cast_build_tree(p, p, 1, 0, 8, 8, p, 10, p, p, p, p, p, nul, nul, nul, nul, nul, nul, None) == -2
+    assert L.cast_build_tree(p, p, 1, 65, 8, 8, p, 10, p, p, p, p, p, nul, nul, nul, nul, nul, nul, None) == -2
+    assert L.cast_build_tree(p, p, 1, 15, 8, 0, p, 10, p, p, p, p, p, nul, nul, nul, nul, nul, nul, None) == -8
+    assert L.cast_build_tree(p, p, 1, 15, 8, 8, p, 2000, p, p, p, p, p, nul, nul, nul, nul, nul, nul, None) == -2
+    # pack outputs without cu_q, pack tokens without roots
+    assert L.cast_build_tree(p, p, 1, 15, 8, 8, p, 10, p, p, p, p, p, nul, p, nul, nul, nul, nul, None) == -1
+    assert L.cast_build_tree(p, p, 1, 15, 8, 8, p, 10, p, p, p, p, p, p, nul, nul, p, nul, nul, None) == -1
+    assert L.cast_build_tree(p, p, 0, 15, 8, 8, p, 10, p, p, p, p, p, nul, nul, nul, nul, nul, nul, None) == 0

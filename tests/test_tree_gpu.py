@@ -1,0 +1,145 @@
+"""GPU tree construction against the reference's own outputs and the oracle.
+
+Bar: token / depth / parent arrays identical; top-k indices identical;
+log-probs and scores within 1e-12 relative (the GPU's log-sum-exp can differ
+from numpy's pairwise sum in the last bits). build_tree on the reference's own
+top-k arrays is bit-exact in every field, scores included, since it performs
+the reference's float64 operations in the reference's order.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cast_b200
+from cast_b200 import _lib, workloads
+from oracle import tree as otree
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-12
+
+
+def _lp_close(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    assert a.shape == b.shape
+    fin = np.isfinite(b)
+    assert np.array_equal(np.isfinite(a), fin)
+    assert np.all(np.abs(a[fin] - b[fin]) <= RTOL * np.maximum(1.0, np.abs(b[fin])))
+
+
+def test_block_topk_config1(cuda, golden):
+    g = golden("tree_cfg1.npz")
+    idx, lp = cast_b200.block_topk(np.random.default_rng(0).normal(scale=5, size=(15, 64)))
+    assert np.array_equal(idx, g["idx"])
+    _lp_close(lp, g["lp"])
+
+
+def test_build_tree_config1_bit_exact(cuda, golden):
+    g = golden("tree_cfg1.npz")
+    for n in (16, 127):
+        nodes = cast_b200.build_tree(g["idx"], g["lp"], n)
+        assert [nd.token for nd in nodes] == g[f"n{n}_token"].tolist()
+        assert [nd.depth for nd in nodes] == g[f"n{n}_depth"].tolist()
+        assert [nd.parent for nd in nodes] == g[f"n{n}_parent"].tolist()
+        assert np.array_equal(np.array([nd.score for nd in nodes]), g[f"n{n}_score"])
+
+
+def test_golden_tree_cases(cuda, golden):
+    g = golden("tree_cases.npz")
+    for name, (seed, L, V, k, budget) in zip(g["names"], g["params"]):
+        k, budget = int(k), int(budget)
+        idx, lp = cast_b200.block_topk(g[f"{name}_logits"], max(k, 1))
+        assert np.array_equal(idx, g[f"{name}_idx"]), name
+        _lp_close(lp, g[f"{name}_lp"])
+        nodes = cast_b200.build_tree(g[f"{name}_idx"], g[f"{name}_lp"], budget, k)
+        assert [nd.token for nd in nodes] == g[f"{name}_token"].tolist(), name
+        assert [nd.depth for nd in nodes] == g[f"{name}_depth"].tolist(), name
+        assert [nd.parent for nd in nodes] == g[f"{name}_parent"].tolist(), name
+        assert np.array_equal(np.array([nd.score for nd in nodes], dtype=np.float64), g[f"{name}_score"]), name
+
+
+def test_full_vocab_rows(cuda, golden):
+    g = golden("topk_vocab.npz")
+    for name in ("v151936", "v128256"):
+        V = int(name[1:])
+        x = np.random.default_rng(list(g[f"{name}_seed"])).normal(scale=5, size=(15, V))
+        idx, lp = cast_b200.block_topk(x)
+        assert np.array_equal(idx, g[f"{name}_idx"])
+        _lp_close(lp, g[f"{name}_lp"])
+        nodes = cast_b200.build_tree(idx, lp, 127)
+        assert [nd.parent for nd in nodes] == g[f"{name}_n127_parent"].tolist()
+        assert [nd.token for nd in nodes] == g[f"{name}_n127_token"].tolist()
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_with_ties_against_oracle(cuda, seed):
+    rng = np.random.default_rng(500 + seed)
+    B = int(rng.integers(1, 6))
+    L = int(rng.integers(1, 16))
+    V = int(rng.integers(2, 3000))
+    k = int(rng.integers(1, min(V, 24) + 1))
+    budget = int(rng.integers(0, 400))
+    x = rng.normal(scale=float(rng.choice([0.5, 2.0, 5.0])), size=(B, L, V))
+    if seed % 3 == 0:
+        x = np.round(x)
+    xd = torch.from_numpy(x).to(cuda)
+    idx, lp = cast_b200.block_topk_device(xd, k)
+    trees = cast_b200.build_trees(idx, lp, budget, k)
+    assert _lib.device_error() == 0
+    for b in range(B):
+        oi, ol = otree.block_topk(x[b], k)
+        assert np.array_equal(idx[b].cpu().numpy(), oi)
+        _lp_close(lp[b].cpu().numpy(), ol)
+        ref = otree.build_tree(oi, ol, budget, k)
+        n = int(trees.count[b])
+        assert n == len(ref)
+        assert np.array_equal(trees.token[b, :n].cpu().numpy(), ref.token)
+        assert np.array_equal(trees.depth[b, :n].cpu().numpy(), ref.depth)
+        assert np.array_equal(trees.parent[b, :n].cpu().numpy(), ref.parent)
+        _lp_close(trees.score[b, :n].cpu().numpy(), ref.score)
+
+
+def test_pack_layout_matches_serving_convention(cuda):
+    # the pack arrays of cast_trees/serving.py:213-222, built in the same launch
+    w = workloads.Workload("t", 9, 500, [100, 7, 33], [16, 40, 1])
+    logits = torch.from_numpy(w.logits_batch()).to(cuda)
+    idx, lp = cast_b200.block_topk_device(logits, 8)
+    lay = w.layout()
+    roots = torch.tensor([3, 4, 5], dtype=torch.int32, device=cuda)
+    budget = torch.tensor(w.N, dtype=torch.int32, device=cuda)
+    t = cast_b200.build_trees(idx, lp, budget, 8, cu_q=torch.from_numpy(lay["cu_q"]), root_token=roots,
+                              seq_len=torch.tensor(w.S, dtype=torch.int32))
+    assert _lib.device_error() == 0
+    for b in range(w.B):
+        oi, ol = otree.block_topk(w.logits(b))
+        ref = otree.build_tree(oi, ol, w.N[b])
+        q0, q1 = lay["cu_q"][b], lay["cu_q"][b + 1]
+        assert t.pack_parent[q0:q1].cpu().tolist() == otree.pack_parent(ref.parent).tolist()
+        assert t.pack_token[q0:q1].cpu().tolist() == [3 + b] + ref.token.tolist()
+        assert t.pack_pos[q0:q1].cpu().tolist() == [w.S[b]] + (w.S[b] + ref.depth).tolist()
+
+
+def test_config3_rows_bit_exact(cuda):
+    # BASELINE config 3 block scores (V = 128256): GPU tree arrays equal the reference's
+    w = workloads.config(3)
+    sub = w.shard([0, 1, 2])
+    logits = torch.from_numpy(sub.logits_batch()).to(cuda)
+    idx, lp = cast_b200.block_topk_device(logits, 8)
+    t = cast_b200.build_trees(idx, lp, 127, 8)
+    assert _lib.device_error() == 0
+    for b in range(sub.B):
+        oi, ol = otree.block_topk(sub.logits(b))
+        assert np.array_equal(idx[b].cpu().numpy(), oi)
+        ref = otree.build_tree(oi, ol, 127)
+        assert np.array_equal(t.token[b].cpu().numpy(), ref.token)
+        assert np.array_equal(t.parent[b].cpu().numpy(), ref.parent)
+        assert np.array_equal(t.depth[b].cpu().numpy(), ref.depth)
+        _lp_close(t.score[b].cpu().numpy(), ref.score)
+
+
+def test_host_argument_errors(cuda):
+    x = torch.randn(2, 5, device=cuda, dtype=torch.float64)
+    with pytest.raises(_lib.CastError):
+        cast_b200.block_topk_device(x, 6)          # k > V
+    with pytest.raises(_lib.CastError):
+        cast_b200.block_topk_device(x, 0)
