@@ -109,7 +109,6 @@ const char* cast_strerror(int status) {
     case CAST_ERR_MASK_MODE: return "pass exactly one of anc_words and parent";
     case CAST_DEV_BAD_LAYOUT: return "device: cu_q/cu_kv/prefix_len/pack_len out of range or above max_pack/max_kv";
     case CAST_DEV_BAD_PARENT: return "device: parent array is not a forest in pack order (need -1 <= parent[i] < i, parent[0] = -1)";
-    case CAST_DEV_TOPK_TIE: return "device: equal log-probs straddle the k-th place beyond the candidate margin";
     case CAST_DEV_TIMEOUT: return "device: a bounded wait gave up";
     case CAST_DEV_TREE_OVERFLOW: return "device: budget above max_budget";
     default: return "unknown status";

@@ -9,17 +9,19 @@ namespace cast {
 // ---------------------------------------------------------------------------
 // block_topk (cast_trees/tree.py:20-26).
 //
-// One CTA per row of V logits, one pass over HBM. Each thread keeps
+// One CTA per row of V logits. Pass 1 reads the row once; each thread keeps
 //  * an online (running max m_t, sum_t of exp(x - m_t)) pair, and
-//  * its KC best (x, index) candidates, sorted by x descending; because a thread
-//    visits its elements in increasing index order, an equal x never displaces
-//    an earlier one, which is the stable sort's lower-index-first rule.
-// The CTA merges both, forms lp = (x - M) - log(sum exp(x - M)) with the
-// reference's operation order, and re-sorts the KC best by (lp desc, index
-// asc): the subtraction can make distinct x equal in lp, and the reference
-// sorts on lp. Any element outside the KC candidates has lp <= the KC-th one;
-// it could only enter the top k if the k-th and KC-th lp were equal, which is
-// reported as CAST_DEV_TOPK_TIE instead of returning a possibly different order.
+//  * its KC best (x, index) candidates, sorted by x descending; a thread
+//    visits its elements in increasing index order, so an equal x never
+//    displaces an earlier one (the stable sort's lower-index-first rule).
+// The CTA merges both and forms lp = (x - M) - log(sum exp(x - M)), the
+// reference's operation order. The reference sorts on lp, and the rounding
+// of that subtraction can map distinct x to one lp; so the KC best by x are
+// re-sorted by (lp desc, index asc), which is exact whenever the k-th lp is
+// strictly above the KC-th (no element outside the candidates can then tie
+// into the top k). Otherwise - rows with many equal log-probs - pass 2 reads
+// the row again and selects the top k on lp itself, with M and the log-sum
+// of pass 1: exact in every case.
 // ---------------------------------------------------------------------------
 namespace topk {
 constexpr int NT = 256;
@@ -57,7 +59,7 @@ struct CandList {
   }
 };
 
-// (a_x, a_i) ranks before (b_x, b_i): larger x, then smaller index; empty last.
+// (a_x, a_i) ranks before (b_x, b_i): larger value, then smaller index; empty last.
 __device__ __forceinline__ bool cand_before(double ax, int ai, double bx, int bi) {
   if (ai < 0) return false;
   if (bi < 0) return true;
@@ -74,24 +76,11 @@ __device__ __forceinline__ void online_add(double& m, double& s, double v) {
   }
 }
 
-template <int KC, bool VEC2>
-__global__ void __launch_bounds__(topk::NT)
-block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
-                  int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
+// Visits the row in each thread's increasing index order: f(value, index).
+template <bool VEC2, typename F>
+__device__ __forceinline__ void scan_row(const double* x, int64_t V, F&& f) {
   using namespace topk;
-  __shared__ double s_m[NW], s_s[NW];
-  __shared__ double s_cx[NW * KC];
-  __shared__ int s_ci[NW * KC];
-  __shared__ double s_fx[KC], s_flp[KC];
-  __shared__ int s_fi[KC];
-
-  const int64_t row = blockIdx.x;
-  const double* x = logits + row * row_stride;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-
-  CandList<KC> cl;
-  cl.init();
-  double m = -INFINITY, s = 0.0;
+  const int tid = threadIdx.x;
   if (VEC2) {
     const double2* x2 = reinterpret_cast<const double2*>(x);
     const int64_t n2 = V >> 1;
@@ -103,42 +92,29 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int j = (int)(2 * (i + u * NT));
-        online_add(m, s, v[u].x); cl.offer(v[u].x, j);
-        online_add(m, s, v[u].y); cl.offer(v[u].y, j + 1);
+        f(v[u].x, j);
+        f(v[u].y, j + 1);
       }
     }
     for (; i < n2; i += NT) {
       const double2 v = __ldcs(x2 + i);
       const int j = (int)(2 * i);
-      online_add(m, s, v.x); cl.offer(v.x, j);
-      online_add(m, s, v.y); cl.offer(v.y, j + 1);
+      f(v.x, j);
+      f(v.y, j + 1);
     }
-    if ((V & 1) && tid == 0) {
-      const double v = x[V - 1];
-      online_add(m, s, v); cl.offer(v, (int)(V - 1));
-    }
+    if ((V & 1) && tid == 0) f(x[V - 1], (int)(V - 1));
   } else {
-    for (int64_t i = tid; i < V; i += NT) {
-      const double v = x[i];
-      online_add(m, s, v); cl.offer(v, (int)i);
-    }
+    for (int64_t i = tid; i < V; i += NT) f(x[i], (int)i);
   }
+}
 
-  // (m, s) reduction: warp, then CTA
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    const double om = __shfl_xor_sync(0xffffffffu, m, off);
-    const double os = __shfl_xor_sync(0xffffffffu, s, off);
-    const double mm = fmax(m, om);
-    if (mm != -INFINITY) {
-      s = (m == -INFINITY ? 0.0 : s * exp(m - mm)) + (om == -INFINITY ? 0.0 : os * exp(om - mm));
-    }
-    m = mm;
-  }
-  if (lane == 0) { s_m[warp] = m; s_s[warp] = s; }
-
-  // candidate tournament inside each warp: KC rounds of a warp arg-best
-  for (int rnd = 0; rnd < KC; ++rnd) {
+// Merges every thread's sorted list into s_out_* (the CTA's KC best, best first).
+template <int KC>
+__device__ __forceinline__ void merge_lists(CandList<KC>& cl, double* s_cx, int* s_ci, double* s_out_x,
+                                            int* s_out_i) {
+  using namespace topk;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int rnd = 0; rnd < KC; ++rnd) {       // warp level: KC rounds of an arg-best
     double bx = cl.x[0];
     int bi = cl.idx[0];
     int bl = lane;
@@ -153,23 +129,12 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
     if (lane == 0) { s_cx[warp * KC + rnd] = bx; s_ci[warp * KC + rnd] = bi; }
   }
   __syncthreads();
-
-  if (warp == 0) {
-    double M = s_m[0];
-    for (int w = 1; w < NW; ++w) M = fmax(M, s_m[w]);
-    double S = 0.0;
-    for (int w = 0; w < NW; ++w)
-      if (s_m[w] != -INFINITY) S += s_s[w] * exp(s_m[w] - M);
-    const double lse = log(S);
-
-    // merge the NW sorted warp lists (KC rounds, each lane scans NW*KC/32 slots)
+  if (warp == 0) {                            // CTA level, over the NW warp lists
     for (int rnd = 0; rnd < KC; ++rnd) {
       double bx = -INFINITY;
       int bi = -1, bslot = -1;
       for (int c = lane; c < NW * KC; c += 32) {
-        if (cand_before(s_ci[c] >= 0 ? s_cx[c] : -INFINITY, s_ci[c], bx, bi)) {
-          bx = s_cx[c]; bi = s_ci[c]; bslot = c;
-        }
+        if (cand_before(s_cx[c], s_ci[c], bx, bi)) { bx = s_cx[c]; bi = s_ci[c]; bslot = c; }
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
@@ -179,37 +144,104 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
         if (cand_before(ox, oi, bx, bi)) { bx = ox; bi = oi; bslot = os; }
       }
       if (lane == 0) {
-        s_fx[rnd] = bx;
-        s_fi[rnd] = bi;
+        s_out_x[rnd] = bx;
+        s_out_i[rnd] = bi;
         if (bslot >= 0) s_ci[bslot] = -1;  // taken
       }
       __syncwarp();
     }
-    if (lane == 0) {
-      int n = 0;
-      for (int c = 0; c < KC; ++c) {
-        if (s_fi[c] < 0) break;
-        s_flp[c] = (s_fx[c] - M) - lse;
-        ++n;
+  }
+  __syncthreads();
+}
+
+template <int KC, bool VEC2>
+__global__ void __launch_bounds__(topk::NT)
+block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
+                  int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
+  using namespace topk;
+  __shared__ double s_m[NW], s_s[NW];
+  __shared__ double s_cx[NW * KC];
+  __shared__ int s_ci[NW * KC];
+  __shared__ double s_fx[KC], s_flp[KC];
+  __shared__ int s_fi[KC];
+  __shared__ double s_M, s_lse;
+  __shared__ int s_pass2;
+
+  const int64_t row = blockIdx.x;
+  const double* x = logits + row * row_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  CandList<KC> cl;
+  cl.init();
+  double m = -INFINITY, s = 0.0;
+  scan_row<VEC2>(x, V, [&](double v, int j) {
+    online_add(m, s, v);
+    cl.offer(v, j);
+  });
+
+  // (m, s): warp, then CTA
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const double om = __shfl_xor_sync(0xffffffffu, m, off);
+    const double os = __shfl_xor_sync(0xffffffffu, s, off);
+    const double mm = fmax(m, om);
+    if (mm != -INFINITY) {
+      s = (m == -INFINITY ? 0.0 : s * exp(m - mm)) + (om == -INFINITY ? 0.0 : os * exp(om - mm));
+    }
+    m = mm;
+  }
+  if (lane == 0) { s_m[warp] = m; s_s[warp] = s; }
+  merge_lists<KC>(cl, s_cx, s_ci, s_fx, s_fi);
+
+  if (tid == 0) {
+    double M = s_m[0];
+    for (int w = 1; w < NW; ++w) M = fmax(M, s_m[w]);
+    double S = 0.0;
+    for (int w = 0; w < NW; ++w)
+      if (s_m[w] != -INFINITY) S += s_s[w] * exp(s_m[w] - M);
+    const double lse = log(S);
+    s_M = M;
+    s_lse = lse;
+    int n = 0;
+    for (int c = 0; c < KC; ++c) {
+      if (s_fi[c] < 0) break;
+      s_flp[c] = (s_fx[c] - M) - lse;
+      ++n;
+    }
+    // stable insertion sort by (lp desc, index asc)
+    for (int a = 1; a < n; ++a) {
+      const double lv = s_flp[a];
+      const int iv = s_fi[a];
+      int c = a - 1;
+      while (c >= 0 && (s_flp[c] < lv || (s_flp[c] == lv && s_fi[c] > iv))) {
+        s_flp[c + 1] = s_flp[c];
+        s_fi[c + 1] = s_fi[c];
+        --c;
       }
-      // stable insertion sort by (lp desc, index asc)
-      for (int a = 1; a < n; ++a) {
-        const double lv = s_flp[a];
-        const int iv = s_fi[a];
-        int c = a - 1;
-        while (c >= 0 && (s_flp[c] < lv || (s_flp[c] == lv && s_fi[c] > iv))) {
-          s_flp[c + 1] = s_flp[c];
-          s_fi[c + 1] = s_fi[c];
-          --c;
-        }
-        s_flp[c + 1] = lv;
-        s_fi[c + 1] = iv;
-      }
-      if (V > KC && n == KC && s_flp[k - 1] == s_flp[KC - 1]) report(CAST_DEV_TOPK_TIE);
+      s_flp[c + 1] = lv;
+      s_fi[c + 1] = iv;
+    }
+    const bool tie = V > KC && n == KC && s_flp[k - 1] == s_flp[KC - 1];
+    s_pass2 = tie ? 1 : 0;
+    if (!tie) {
       for (int c = 0; c < k; ++c) {
         top_idx[row * k + c] = c < n ? (int64_t)s_fi[c] : (int64_t)0;
         top_lp[row * k + c] = c < n ? s_flp[c] : -INFINITY;
       }
+    }
+  }
+  __syncthreads();
+  if (!s_pass2) return;
+
+  // pass 2: select on lp directly (rows whose boundary log-prob is tied)
+  const double M = s_M, lse = s_lse;
+  cl.init();
+  scan_row<VEC2>(x, V, [&](double v, int j) { cl.offer((v - M) - lse, j); });
+  merge_lists<KC>(cl, s_cx, s_ci, s_flp, s_fi);
+  if (tid == 0) {
+    for (int c = 0; c < k; ++c) {
+      top_idx[row * k + c] = s_fi[c] >= 0 ? (int64_t)s_fi[c] : (int64_t)0;
+      top_lp[row * k + c] = s_fi[c] >= 0 ? s_flp[c] : -INFINITY;
     }
   }
 }

@@ -54,7 +54,6 @@ enum cast_status {
   /* device-side codes (positive), reported by cast_device_error() */
   CAST_DEV_BAD_LAYOUT = 1,    /* cu/prefix/pack arrays out of range or above max_pack/max_kv */
   CAST_DEV_BAD_PARENT = 2,    /* parent[i] >= i or < -1 (or parent[0] != -1) */
-  CAST_DEV_TOPK_TIE = 3,      /* more equal log-probs at the k-th place than the candidate margin */
   CAST_DEV_TIMEOUT = 4,       /* a bounded wait inside a kernel gave up */
   CAST_DEV_TREE_OVERFLOW = 5  /* build_tree budget above max_budget */
 };
