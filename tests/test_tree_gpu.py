@@ -73,6 +73,12 @@ def test_full_vocab_rows(cuda, golden):
 
 @pytest.mark.parametrize("seed", range(12))
 def test_random_with_ties_against_oracle(cuda, seed):
+    # Every third case rounds the logits to integers: equal log-probs and equal
+    # path scores everywhere. There the heap's tie order depends on the last
+    # bit of each lp, and numpy's own lse (SIMD exp, pairwise sum) is not
+    # reproducible bit for bit across machines; so the tree kernel is checked
+    # bit-exact on the lp it was given, and the whole pipeline against the pure
+    # oracle on the continuous cases.
     rng = np.random.default_rng(500 + seed)
     B = int(rng.integers(1, 6))
     L = int(rng.integers(1, 16))
@@ -80,7 +86,8 @@ def test_random_with_ties_against_oracle(cuda, seed):
     k = int(rng.integers(1, min(V, 24) + 1))
     budget = int(rng.integers(0, 400))
     x = rng.normal(scale=float(rng.choice([0.5, 2.0, 5.0])), size=(B, L, V))
-    if seed % 3 == 0:
+    tied = seed % 3 == 0
+    if tied:
         x = np.round(x)
     xd = torch.from_numpy(x).to(cuda)
     idx, lp = cast_b200.block_topk_device(xd, k)
@@ -88,15 +95,21 @@ def test_random_with_ties_against_oracle(cuda, seed):
     assert _lib.device_error() == 0
     for b in range(B):
         oi, ol = otree.block_topk(x[b], k)
-        assert np.array_equal(idx[b].cpu().numpy(), oi)
-        _lp_close(lp[b].cpu().numpy(), ol)
-        ref = otree.build_tree(oi, ol, budget, k)
+        gi, gl = idx[b].cpu().numpy(), lp[b].cpu().numpy()
+        assert np.array_equal(gi, oi)
+        _lp_close(gl, ol)
         n = int(trees.count[b])
-        assert n == len(ref)
-        assert np.array_equal(trees.token[b, :n].cpu().numpy(), ref.token)
-        assert np.array_equal(trees.depth[b, :n].cpu().numpy(), ref.depth)
-        assert np.array_equal(trees.parent[b, :n].cpu().numpy(), ref.parent)
-        _lp_close(trees.score[b, :n].cpu().numpy(), ref.score)
+        same_lp = otree.build_tree(gi, gl, budget, k)     # the oracle on the GPU's own lp
+        assert n == len(same_lp)
+        assert np.array_equal(trees.token[b, :n].cpu().numpy(), same_lp.token)
+        assert np.array_equal(trees.depth[b, :n].cpu().numpy(), same_lp.depth)
+        assert np.array_equal(trees.parent[b, :n].cpu().numpy(), same_lp.parent)
+        assert np.array_equal(trees.score[b, :n].cpu().numpy(), same_lp.score)
+        if not tied:
+            ref = otree.build_tree(oi, ol, budget, k)
+            assert np.array_equal(trees.token[b, :n].cpu().numpy(), ref.token)
+            assert np.array_equal(trees.parent[b, :n].cpu().numpy(), ref.parent)
+            _lp_close(trees.score[b, :n].cpu().numpy(), ref.score)
 
 
 def test_pack_layout_matches_serving_convention(cuda):
