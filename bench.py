@@ -186,8 +186,9 @@ def run_cast(args):
                                   w.layout()["max_pack"], w.layout()["max_kv"])
     st.ws = torch.empty(max(ws, 1), dtype=torch.uint8, device=dev)
 
-    # launches per step: block_topk + build_tree + attention (+ combine when split)
-    attn_launches = 2 if ws > 0 else 1
+    # launches per step: block_topk + build_tree + attention (+ combine when the keys are split)
+    kernel, n_split, attn_launches = cast_b200.attention_plan(st.q, st.k, st.v, st.out, w.B, w.layout()["max_pack"],
+                                                              w.layout()["max_kv"])
     launches_per_step = 2 + attn_launches
 
     for _ in range(args.warmup):
@@ -284,6 +285,7 @@ def run_cast(args):
                    "global_batch": B_PER_RANK * world, "seq_len": "4096-8192 (ragged)",
                    "parallelism": f"sequence-sharded x{world}, no collective",
                    "l2": "inputs larger than L2 (logits 0.98 GB + K/V 1.59 GB streamed per step)"},
+        "attn_kernel": kernel, "attn_key_splits": n_split,
         "us_per_call": round(attn_ms * 1e3, 1),
         "attn_tflops_per_gpu": round(attn_tflops, 2),
         "attn_gbs_per_gpu": round(attn_gbs, 1),

@@ -1,0 +1,397 @@
+// Tensor-core (tcgen05 / TMEM / TMA) ragged tree attention for 16-bit inputs, D = 128.
+//
+// Work unit (one CTA, one per SM): sequence b, KV head h, up to two 128-row
+// query tiles of the G*P_b rows of that head group (row r = pack token r / G,
+// query head h*G + r % G; both tiles share every K/V tile), and a chunk of the
+// key range [0, S_b + P_b) (the whole range unless the launch splits keys).
+//
+// Roles (12 warps):
+//   warp 0      TMEM allocation; lane 0 issues the TMA loads: the Q tiles once,
+//               then 128-key K and V tiles into a 2-stage ring.
+//   warp 1      lane 0 issues every tcgen05.mma:
+//                 S_q  = Q_q K_j^T    (A, B in shared memory, K-major)
+//                 O_q += P_q V_j      (A = P in tensor memory, B = V MN-major)
+//               in the order QK0_j, PV1_{j-1}, QK1_j, PV0_j, so that the
+//               softmax of one tile overlaps the tensor core on the other.
+//   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: thread t owns
+//               TMEM lane t (query row t). Per key tile: row max from S, lazy
+//               rescale of O (only when the max grew by more than 2^8), then
+//               P = exp2(S*c - m) rounded to 16 bits and stored into the first
+//               64 columns of S (tcgen05.st), which the PV MMA reads.
+// Tensor memory (512 columns): S_0, S_1 (128 fp32 columns each), O_0, O_1.
+// Visibility: keys < S_b always; pack key S_b + j iff bit j of the row token's
+// ancestor bitset (shared memory; built from `parent` or copied); keys past
+// the chunk end are masked (TMA fills rows past the tensor with zeros and the
+// next sequence's rows are masked out). Every mbarrier wait is bounded; on
+// expiry the CTA records CAST_DEV_TIMEOUT, lets in-flight copies and MMAs
+// drain, frees its tensor memory and returns.
+#pragma once
+
+#include "attn_simt.cuh"
+#include "tc_common.cuh"
+
+namespace cast {
+namespace tca {
+
+constexpr int BM = 128;           // rows per query tile
+constexpr int QT = 2;             // query tiles per CTA
+constexpr int BN = 128;           // keys per K/V tile
+constexpr int D = 128;
+constexpr int NST = 2;            // K/V ring stages
+constexpr int NT = 384;           // threads
+constexpr int TILE_BYTES = BN * D * 2;        // 32 KB: one 128 x 128 16-bit tile
+constexpr int HALF_BYTES = TILE_BYTES / 2;    // 16 KB: 64-column half (one 128B-swizzle panel)
+constexpr int SMEM_Q = 0;
+constexpr int SMEM_K = SMEM_Q + QT * TILE_BYTES;
+constexpr int SMEM_V = SMEM_K + NST * TILE_BYTES;
+constexpr int SMEM_ANC = SMEM_V + NST * TILE_BYTES;   // 196608
+constexpr float kRescaleLog2 = 8.0f;          // lazy O rescale threshold (factor 256)
+
+__host__ __device__ inline int anc_tokens(int G) { return QT * BM / G + 2; }
+__host__ __device__ inline size_t smem_bytes(int G, int W) {
+  return 1024 + SMEM_ANC + (size_t)anc_tokens(G) * W * sizeof(uint64_t);
+}
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[NST], k_empty[NST], v_full[NST], v_empty[NST];
+  uint64_t s_full[QT], p_full[QT];
+  uint64_t o_full;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(NT, 1)
+attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV) {
+  using namespace tc;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* sAnc = reinterpret_cast<uint64_t*>(smem + SMEM_ANC);
+  __shared__ __align__(8) Bars bars;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.y / p.H_kv, h = blockIdx.y % p.H_kv;
+  const SeqMeta m = load_seq(p.cu_q, p.cu_kv, p.prefix_len, p.pack_len, b, p.total_q, p.total_kv, p.max_pack,
+                             p.max_kv);
+  if (!m.ok) {
+    if (tid == 0 && blockIdx.x == 0 && blockIdx.z == 0) report(CAST_DEV_BAD_LAYOUT);
+    return;
+  }
+  const int G = p.G;
+  const int rows = G * m.P;
+  const int r_base = blockIdx.x * (QT * BM);
+  if (r_base >= rows) return;
+  const int n_qt = (rows - r_base > BM) ? 2 : 1;
+  const int nkeys = m.S + m.P;
+  const int k_begin = blockIdx.z * p.chunk;
+  if (k_begin >= nkeys) return;
+  const int k_end = min(nkeys, k_begin + p.chunk);
+  const int n_kt = (k_end - k_begin + BN - 1) / BN;
+  volatile int* abort_flag = &abort_sh;
+
+  if (tid == 0) {
+    mbar_init(smem_u32(&bars.q_full), 1);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(smem_u32(&bars.k_full[s]), 1);
+      mbar_init(smem_u32(&bars.k_empty[s]), 1);
+      mbar_init(smem_u32(&bars.v_full[s]), 1);
+      mbar_init(smem_u32(&bars.v_empty[s]), 1);
+    }
+    for (int q = 0; q < QT; ++q) {
+      mbar_init(smem_u32(&bars.s_full[q]), 1);
+      mbar_init(smem_u32(&bars.p_full[q]), BM);
+    }
+    mbar_init(smem_u32(&bars.o_full), 1);
+    abort_sh = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 0) tmem_alloc(smem_u32(&tmem_base_sh), 512);
+  const int i_lo = r_base / G;
+  const int i_hi = min(m.P - 1, (r_base + QT * BM - 1) / G);
+  if (k_end > m.S) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint32_t qf = smem_u32(&bars.q_full);
+      mbar_expect_tx(qf, n_qt * TILE_BYTES);
+      for (int q = 0; q < n_qt; ++q) {
+        const int tok = m.q0 + (r_base + q * BM) / G;
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d(smem_u32(smem + SMEM_Q + q * TILE_BYTES + hf * HALF_BYTES), &tmQ, hf * 64, h * G, tok, qf);
+      }
+      int issued = 0;
+      for (int j = 0; j < n_kt; ++j) {
+        const int s = j % NST;
+        const uint32_t use = (uint32_t)(j / NST);
+        const int row = m.kv0 + k_begin + j * BN;
+        if (j >= NST && !mbar_wait(smem_u32(&bars.k_empty[s]), (use - 1) & 1, abort_flag)) break;
+        mbar_expect_tx(smem_u32(&bars.k_full[s]), TILE_BYTES);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d(smem_u32(smem + SMEM_K + s * TILE_BYTES + hf * HALF_BYTES), &tmK, hf * 64, h, row,
+                      smem_u32(&bars.k_full[s]));
+        if (j >= NST && !mbar_wait(smem_u32(&bars.v_empty[s]), (use - 1) & 1, abort_flag)) {
+          issued = j + 1;  // K of tile j is in flight
+          break;
+        }
+        mbar_expect_tx(smem_u32(&bars.v_full[s]), TILE_BYTES);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d(smem_u32(smem + SMEM_V + s * TILE_BYTES + hf * HALF_BYTES), &tmV, hf * 64, h, row,
+                      smem_u32(&bars.v_full[s]));
+        issued = j + 1;
+      }
+      // let the last copies land before the CTA can exit (immediate on the normal path)
+      for (int j = max(0, issued - NST); j < issued; ++j) {
+        const int s = j % NST;
+        const uint32_t ph = (uint32_t)(j / NST) & 1;
+        mbar_wait(smem_u32(&bars.k_full[s]), ph, nullptr);
+        mbar_wait(smem_u32(&bars.v_full[s]), ph, nullptr);
+      }
+      mbar_wait(qf, 0, nullptr);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false, false);
+      constexpr uint32_t idesc_pv = idesc_f16(BF16, BM, D, false, true);
+      const uint32_t sQ = smem_u32(smem + SMEM_Q), sK = smem_u32(smem + SMEM_K), sV = smem_u32(smem + SMEM_V);
+      auto qk = [&](int q, int j) {
+        const uint32_t a0 = sQ + q * TILE_BYTES, b0 = sK + (j % NST) * TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * HALF_BYTES + (k & 3) * 32;
+          mma_ss(tmem + q * 128, desc_kmajor(a0 + off), desc_kmajor(b0 + off), idesc_qk, k > 0 ? 1u : 0u);
+        }
+      };
+      auto pv = [&](int q, int j) {
+        const uint32_t b0 = sV + (j % NST) * TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k)
+          mma_ts(tmem + 256 + q * 128, tmem + q * 128 + k * 8, desc_mnmajor(b0 + k * 2048, HALF_BYTES), idesc_pv,
+                 (j > 0 || k > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(smem_u32(&bars.q_full), 0, abort_flag);
+      int j = 0;
+      for (; ok && j < n_kt; ++j) {
+        const int s = j % NST;
+        const uint32_t ph = (uint32_t)(j / NST) & 1;
+        if (!(ok = mbar_wait(smem_u32(&bars.k_full[s]), ph, abort_flag))) break;
+        fence_after_sync();
+        qk(0, j);
+        mma_commit(smem_u32(&bars.s_full[0]));
+        if (n_qt == 2) {
+          if (j > 0) {
+            if (!(ok = mbar_wait(smem_u32(&bars.p_full[1]), (uint32_t)(j - 1) & 1, abort_flag))) break;
+            fence_after_sync();
+            pv(1, j - 1);
+            mma_commit(smem_u32(&bars.v_empty[(j - 1) % NST]));
+          }
+          qk(1, j);
+          mma_commit(smem_u32(&bars.s_full[1]));
+        }
+        mma_commit(smem_u32(&bars.k_empty[s]));
+        if (!(ok = mbar_wait(smem_u32(&bars.v_full[s]), ph, abort_flag))) break;
+        if (!(ok = mbar_wait(smem_u32(&bars.p_full[0]), (uint32_t)j & 1, abort_flag))) break;
+        fence_after_sync();
+        pv(0, j);
+        if (n_qt == 1) mma_commit(smem_u32(&bars.v_empty[s]));
+      }
+      if (ok && n_qt == 2) {
+        if (mbar_wait(smem_u32(&bars.p_full[1]), (uint32_t)(n_kt - 1) & 1, abort_flag)) {
+          fence_after_sync();
+          pv(1, n_kt - 1);
+          mma_commit(smem_u32(&bars.v_empty[(n_kt - 1) % NST]));
+        }
+      }
+      mma_commit(smem_u32(&bars.o_full));  // also on abort: tracks whatever was issued
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int q = (warp - 4) >> 2;
+    const int t = tid - 128 - q * BM;  // == TMEM lane
+    if (q < n_qt) {
+      const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+      const uint32_t S_t = tmem + lane_off + q * 128;
+      const uint32_t O_t = tmem + lane_off + 256 + q * 128;
+      const int r = r_base + q * BM + t;
+      const int li = min(r / G, m.P - 1) - i_lo;
+      const uint64_t* anc = sAnc + (size_t)li * p.W;
+      const float c = p.scale_log2;
+      float m_ref = -INFINITY, l = 0.f;
+      bool ok = true;
+      uint32_t v[32];
+      // Every tcgen05.ld/st below is .sync.aligned: control flow around them is
+      // kept warp-uniform (waits are followed by a warp vote, per-row choices
+      // are made with per-lane values inside uniform branches).
+      for (int j = 0; j < n_kt; ++j) {
+        ok = mbar_wait(smem_u32(&bars.s_full[q]), (uint32_t)j & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        fence_after_sync();
+        const int n0 = k_begin + j * BN;
+        const bool full = (n0 + BN <= m.S) && (n0 + BN <= k_end);
+        uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
+        if (!full) {
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t bits = 0;
+#pragma unroll 1
+            for (int i = 0; i < 32; ++i) {
+              const int n = n0 + cc * 32 + i;
+              bool ok_k = n < k_end;
+              if (ok_k && n >= m.S) {
+                const int jj = n - m.S;
+                ok_k = (anc[jj >> 6] >> (jj & 63)) & 1ull;
+              }
+              bits |= (ok_k ? 1u : 0u) << i;
+            }
+            vis[cc] = bits;
+          }
+        }
+        // pass 1: row max (raw scores; the scale c > 0 is applied once)
+        float mx = -INFINITY;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          tmem_ld32(S_t + cc * 32, v);
+          tmem_ld_wait();
+          if (full) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx = ((vis[cc] >> i) & 1u) ? fmaxf(mx, __uint_as_float(v[i])) : mx;
+          }
+        }
+        const float m_tile = (mx == -INFINITY) ? -INFINITY : mx * c;
+        const bool grow = m_tile > m_ref + kRescaleLog2 || (m_ref == -INFINITY && m_tile != -INFINITY);
+        const bool rescale = grow && m_ref != -INFINITY;
+        const float alpha = rescale ? ex2(m_ref - m_tile) : 1.f;
+        if (grow) m_ref = m_tile;
+        if (__any_sync(0xffffffffu, rescale)) {
+          l *= alpha;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            tmem_ld32(O_t + cc * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            tmem_st32(O_t + cc * 32, v);
+          }
+          tmem_st_wait();
+        }
+        const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+        // pass 2: P = exp2(S*c - m), 16-bit, into the first 64 columns of S
+        float rs = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          tmem_ld32(S_t + cc * 32, v);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float s0 = __uint_as_float(v[2 * i]), s1 = __uint_as_float(v[2 * i + 1]);
+            float p0 = ex2(fmaf(s0, c, -m_use));
+            float p1 = ex2(fmaf(s1, c, -m_use));
+            if (!full) {
+              p0 = ((vis[cc] >> (2 * i)) & 1u) ? p0 : 0.f;
+              p1 = ((vis[cc] >> (2 * i + 1)) & 1u) ? p1 : 0.f;
+            }
+            rs += p0 + p1;
+            pk[i] = pack2<BF16>(p0, p1);
+          }
+          tmem_st16(S_t + cc * 16, pk);
+        }
+        l += rs;
+        tmem_st_wait();
+        fence_before_sync();
+        mbar_arrive(smem_u32(&bars.p_full[q]));
+      }
+      // epilogue: O / l, or the unnormalised partial of this key chunk
+      bool done = mbar_wait(smem_u32(&bars.o_full), 0, ok ? abort_flag : nullptr);
+      done = __all_sync(0xffffffffu, done && ok);
+      fence_after_sync();
+      if (done) {
+        const bool store = r < rows;
+        const int i = min(r / G, m.P - 1), hq = h * G + r % G;
+        const int64_t tq = m.q0 + i;
+        if (p.n_split == 1) {
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+          T* out = static_cast<T*>(p.out) + tq * p.so_m + (int64_t)hq * p.so_h;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            tmem_ld32(O_t + cc * 32, v);
+            tmem_ld_wait();
+            uint32_t pk[16];
+#pragma unroll
+            for (int i2 = 0; i2 < 16; ++i2)
+              pk[i2] = pack2<BF16>(__uint_as_float(v[2 * i2]) * inv, __uint_as_float(v[2 * i2 + 1]) * inv);
+            if (store) {
+              uint4* dst = reinterpret_cast<uint4*>(out + cc * 32);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            }
+          }
+        } else {
+          const int64_t slot = ((int64_t)blockIdx.z * p.total_q + tq) * p.H_q + hq;
+          float* O = p.ws_o + slot * D;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            tmem_ld32(O_t + cc * 32, v);
+            tmem_ld_wait();
+            if (store) {
+              float4* dst = reinterpret_cast<float4*>(O + cc * 32);
+#pragma unroll
+              for (int u = 0; u < 8; ++u)
+                dst[u] = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
+                                     __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+            }
+          }
+          if (store) {
+            p.ws_ml[slot * 2 + 0] = m_ref;
+            p.ws_ml[slot * 2 + 1] = l;
+          }
+        }
+      }
+    }
+  }
+
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  if (warp == 0) {
+    // on the normal path every MMA has completed (o_full); after an abort, wait (bounded) for them
+    mbar_wait(smem_u32(&bars.o_full), 0, nullptr);
+    __syncwarp();
+    tmem_dealloc(tmem, 512);
+    tmem_relinquish();
+  }
+}
+
+}  // namespace tca
+}  // namespace cast

@@ -1,12 +1,15 @@
 // C ABI of cast_b200 (declared in include/cast_b200.h): argument checks, launch
 // planning and kernel dispatch. Everything the library launches is in this
 // translation unit, so the per-device error word is one symbol.
+#include <cudaTypedefs.h>
 #include <math.h>
 #include <stdio.h>
 #include <atomic>
+#include <type_traits>
 
 #include "common.cuh"
 #include "attn_simt.cuh"
+#include "attn_tc.cuh"
 #include "tree_build.cuh"
 
 namespace cast {
@@ -86,6 +89,105 @@ int launch_simt(AttnParams& p, const SimtPlan& pl, cudaStream_t st) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// ---- tensor-core path ---------------------------------------------------------
+// Launch plan: 256-row blocks of each (sequence, KV head); the key range is
+// split only when the grid would not fill the GPU about four times over.
+struct TcPlan {
+  int m_blocks, n_split, chunk, W;
+  size_t ws_bytes;
+};
+
+TcPlan plan_tc(int B, int total_q, int H_q, int H_kv, int max_pack, int max_kv, int sms) {
+  TcPlan pl;
+  const int G = H_q / H_kv;
+  pl.m_blocks = (G * max_pack + tca::QT * tca::BM - 1) / (tca::QT * tca::BM);
+  if (pl.m_blocks < 1) pl.m_blocks = 1;
+  pl.W = (max_pack + 63) / 64;
+  if (pl.W < 1) pl.W = 1;
+  const long long base = (long long)B * H_kv * pl.m_blocks;
+  const long long target = 4LL * (sms > 0 ? sms : 148);
+  const int kv = max_kv > 0 ? max_kv : 1;
+  int chunk = ((kv + tca::BN - 1) / tca::BN) * tca::BN;
+  int n_split = 1;
+  while (base * n_split < target && chunk > 16 * tca::BN) {
+    n_split *= 2;
+    chunk = (((kv + n_split - 1) / n_split + tca::BN - 1) / tca::BN) * tca::BN;
+  }
+  n_split = (kv + chunk - 1) / chunk;
+  pl.n_split = n_split;
+  pl.chunk = chunk;
+  pl.ws_bytes = n_split > 1 ? (size_t)n_split * total_q * H_q * (tca::D + 2) * sizeof(float) : 0;
+  return pl;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::atomic<void*> fn{nullptr};
+  void* f = fn.load(std::memory_order_acquire);
+  if (f) return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || f == nullptr)
+    return nullptr;
+  fn.store(f, std::memory_order_release);
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+}
+
+// 3-D map over a [rows, heads, 128] 16-bit tensor: box = 64 dims x `box_heads` x `box_rows`, 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, int dtype, int64_t rows, int heads, int64_t s_row, int64_t s_head,
+              int box_heads, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {128, (cuuint64_t)heads, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)s_head * 2, (cuuint64_t)s_row * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_heads, (cuuint32_t)box_rows};
+  cuuint32_t es[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = dtype == CAST_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The tensor-core kernel takes 16-bit inputs with D = 128, G dividing 128,
+// 16-byte aligned bases and row/head strides that are multiples of 8 elements.
+bool tc_eligible(int dtype, int D, int G, const int64_t* st, const void* q, const void* k, const void* v,
+                 const void* out) {
+  if (dtype == CAST_F32 || D != 128 || G < 1 || 128 % G != 0) return false;
+  for (int t = 0; t < 4; ++t)
+    if (st[3 * t] % 8 != 0 || st[3 * t + 1] % 8 != 0 || st[3 * t + 2] != 1) return false;
+  return aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(out, 16);
+}
+
+int launch_tc(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  const int G = p.G;
+  if (!make_map(&mq, p.q, dtype, p.total_q, p.H_q, p.sq_m, p.sq_h, G, tca::BM / G) ||
+      !make_map(&mk, p.k, dtype, p.total_kv, p.H_kv, p.sk_m, p.sk_h, 1, tca::BN) ||
+      !make_map(&mv, p.v, dtype, p.total_kv, p.H_kv, p.sv_m, p.sv_h, 1, tca::BN))
+    return CAST_ERR_LAUNCH;
+  p.n_split = pl.n_split;
+  p.chunk = pl.chunk;
+  p.m_tiles = pl.m_blocks;
+  p.W = pl.W;
+  const size_t smem = tca::smem_bytes(G, pl.W);
+  dim3 grid(pl.m_blocks, p.B * p.H_kv, pl.n_split);
+  if (dtype == CAST_BF16) {
+    cudaFuncSetAttribute(tca::attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    tca::attn_tc_kernel<true><<<grid, tca::NT, smem, st>>>(p, mq, mk, mv);
+  } else {
+    cudaFuncSetAttribute(tca::attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    tca::attn_tc_kernel<false><<<grid, tca::NT, smem, st>>>(p, mq, mk, mv);
+  }
+  if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  if (pl.n_split > 1) {
+    const long long warps = (long long)p.total_q * p.H_q;
+    const int blocks = (int)((warps * 32 + 255) / 256);
+    if (dtype == CAST_BF16) attn_combine_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(p);
+    else attn_combine_kernel<__half><<<blocks, 256, 0, st>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  }
+  return CAST_OK;
+}
+
 }  // namespace
 }  // namespace cast
 
@@ -133,8 +235,35 @@ size_t cast_tree_attn_workspace_size(int dtype, int B, int total_q, int H_q, int
                                      int max_pack, int max_kv) {
   (void)dtype;
   if (B <= 0 || total_q <= 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0) return 0;
-  const SimtPlan pl = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sm_count());
-  return pl.ws_bytes;
+  const int sms = sm_count();
+  const SimtPlan pl = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sms);
+  size_t ws = pl.ws_bytes;
+  if (dtype != CAST_F32 && D == 128) {
+    const TcPlan tp = plan_tc(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
+    if (tp.ws_bytes > ws) ws = tp.ws_bytes;
+  }
+  return ws;
+}
+
+int cast_tree_attn_plan(int dtype, int B, int total_q, int H_q, int H_kv, int D, int max_pack, int max_kv,
+                        const int64_t* strides, const void* q, const void* k, const void* v, const void* out,
+                        int* plan) {
+  if (!strides || !plan) return CAST_ERR_NULL;
+  if (dtype != CAST_F32 && dtype != CAST_BF16 && dtype != CAST_F16) return CAST_ERR_DTYPE;
+  if (B < 0 || total_q < 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0) return CAST_ERR_SHAPE;
+  if (D != 64 && D != 128) return CAST_ERR_HEAD_DIM;
+  const int sms = sm_count();
+  if (tc_eligible(dtype, D, H_q / H_kv, strides, q, k, v, out)) {
+    const TcPlan tp = plan_tc(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
+    plan[0] = 1;
+    plan[1] = tp.n_split;
+  } else {
+    const SimtPlan sp = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sms);
+    plan[0] = 0;
+    plan[1] = sp.n_split;
+  }
+  plan[2] = plan[1] > 1 ? 2 : 1;
+  return CAST_OK;
 }
 
 int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, int dtype,
@@ -178,13 +307,22 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
   p.scale_log2 = scale * kLog2e;
   p.max_pack = max_pack; p.max_kv = max_kv;
 
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (tc_eligible(dtype, D, p.G, strides, q, k, v, out)) {
+    const TcPlan tp = plan_tc(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
+    if (tp.ws_bytes > 0) {
+      if (!workspace || workspace_bytes < tp.ws_bytes || !aligned(workspace, 16)) return CAST_ERR_WORKSPACE;
+      p.ws_o = static_cast<float*>(workspace);
+      p.ws_ml = p.ws_o + (size_t)tp.n_split * total_q * H_q * D;
+    }
+    return launch_tc(p, tp, dtype, st);
+  }
   const SimtPlan pl = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sms);
   if (pl.ws_bytes > 0) {
     if (!workspace || workspace_bytes < pl.ws_bytes || !aligned(workspace, 16)) return CAST_ERR_WORKSPACE;
     p.ws_o = static_cast<float*>(workspace);
     p.ws_ml = p.ws_o + (size_t)pl.n_split * total_q * H_q * D;
   }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CAST_F32: return launch_simt<float>(p, pl, st);
     case CAST_BF16: return launch_simt<__nv_bfloat16>(p, pl, st);

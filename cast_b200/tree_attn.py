@@ -44,6 +44,21 @@ def workspace_size(dtype, B, total_q, H_q, H_kv, D, max_pack, max_kv):
                                                         max_pack, max_kv))
 
 
+def attention_plan(q, k, v, out, B, max_pack, max_kv):
+    """(kernel, key splits, launches) that varlen_tree_attention would use.
+
+    kernel is "tcgen05" (tensor-core kernel) or "simt" (CUDA-core kernel).
+    """
+    total_q, H_q, D = q.shape
+    strides = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride(), *out.stride())
+    plan = (ctypes.c_int * 3)()
+    code = _lib.lib().cast_tree_attn_plan(_DTYPES[q.dtype], B, total_q, H_q, k.shape[1], D, max_pack, max_kv,
+                                          ctypes.addressof(strides), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                          out.data_ptr(), ctypes.addressof(plan))
+    _lib.check(code, "cast_tree_attn_plan")
+    return ("tcgen05" if plan[0] == 1 else "simt"), int(plan[1]), int(plan[2])
+
+
 def varlen_tree_attention(q, k, v, cu_q, cu_kv, prefix_len, pack_len, ancestor_mask=None, sm_scale=None,
                           *, parent=None, max_pack=None, max_kv=None, out=None, workspace=None):
     """q: [total_q, H_q, D], k/v: [total_kv, H_kv, D] -> [total_q, H_q, D] (q's dtype).

@@ -118,6 +118,16 @@ size_t cast_tree_attn_workspace_size(int dtype, int B, int total_q, int H_q, int
                                      int max_pack, int max_kv);
 
 /*
+ * How cast_tree_attn_fwd would run for these arguments (pure host arithmetic):
+ * plan[0] = 1 for the tcgen05 tensor-core kernel, 0 for the CUDA-core kernel;
+ * plan[1] = number of key-range splits; plan[2] = kernel launches per call
+ * (2 when split partials are merged by the combine kernel).
+ */
+int cast_tree_attn_plan(int dtype, int B, int total_q, int H_q, int H_kv, int D, int max_pack, int max_kv,
+                        const int64_t* strides, const void* q, const void* k, const void* v, const void* out,
+                        int* plan);
+
+/*
  * Per-row fp64 log-softmax and top-k, bit-compatible with
  * cast_trees/tree.py:20-26 block_topk: ties keep the lower index first.
  * logits: float64 [n_rows, V] with row stride `row_stride` (elements).

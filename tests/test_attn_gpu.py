@@ -209,3 +209,42 @@ def test_host_argument_errors(cuda):
                                         torch.zeros(4, dtype=torch.int64, device=cuda))
     with pytest.raises(ValueError):
         cast_b200.varlen_tree_attention(q, k[:, :2], k[:, :2], i32([0, 4]), i32([0, 4]), i32([0]), i32([4]), None)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (8, 8), (16, 8), (32, 4), (64, 4)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tensor_core_kernel_shapes(cuda, Hq, Hkv, dtype):
+    # ragged edge cases on the tcgen05 path: a pure pack (S = 0), a one-token
+    # pack, a prefix that ends inside a key tile, row blocks with one query
+    # tile, and packs wider than 64 tokens
+    S_list = [0, 1, 127, 129, 700, 64, 2000]
+    P_list = [70, 1, 33, 128, 300, 129, 17]
+    sc = _tree_scenario(21, len(S_list), S_list, P_list, Hq=Hq, Hkv=Hkv, D=128)
+    q, k, v = (sc[n].to(cuda, dtype) for n in ("q", "k", "v"))
+    kind, _, _ = cast_b200.attention_plan(q, k, v, torch.empty_like(q), len(S_list), max(P_list),
+                                          max(s + p for s, p in zip(S_list, P_list)))
+    assert kind == "tcgen05"
+    got = _run(sc, dtype, cuda, "parent").float().cpu()
+    err = (got - _oracle(sc, dtype)).abs().max().item()
+    assert err < TOL[dtype], err
+
+
+def test_tensor_core_and_cuda_core_agree(cuda):
+    # the same bf16 problem through both kernels (a non-multiple-of-8 head
+    # stride sends the second call to the CUDA-core kernel)
+    sc = _tree_scenario(22, 4, [1000, 37, 4096, 5], [128, 64, 100, 1], Hq=32, Hkv=8)
+    q, k, v = (sc[n].to(cuda, torch.bfloat16) for n in ("q", "k", "v"))
+    args = (sc["cu_q"].to(cuda), sc["cu_kv"].to(cuda), torch.as_tensor(sc["prefix"]).to(cuda),
+            torch.as_tensor(sc["pack"]).to(cuda), None)
+    par = torch.as_tensor(sc["parent"]).to(cuda)
+    a = cast_b200.varlen_tree_attention(q, k, v, *args, parent=par)
+    kpad = torch.zeros(k.shape[0], 8, 132, dtype=k.dtype, device=cuda)
+    kpad[:, :, :128] = k
+    k2 = kpad[:, :, :128]
+    assert cast_b200.attention_plan(q, k2, v, a, 4, 128, 4196)[0] == "simt"
+    b = cast_b200.varlen_tree_attention(q, k2, v, *args, parent=par)
+    assert _lib.device_error() == 0
+    ref = _oracle(sc, torch.bfloat16)
+    assert (a.float().cpu() - ref).abs().max().item() < 2e-2
+    assert (b.float().cpu() - ref).abs().max().item() < 2e-2
+    assert (a.float() - b.float()).abs().max().item() < 2e-2
