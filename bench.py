@@ -79,7 +79,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -204,15 +204,16 @@ def run_cast(args):
     stream = torch.cuda.current_stream()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(local).__enter__()      # sampled over both timed regions below
+    time.sleep(0.3)                            # nvidia-smi start-up
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t0.record(stream)
-        for i in range(args.steps):
-            st.run(evs[i])
-        t1.record(stream)
-        torch.cuda.synchronize()
+    t0.record(stream)
+    for i in range(args.steps):
+        st.run(evs[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     step_ms = t0.elapsed_time(t1) / args.steps
@@ -242,6 +243,7 @@ def run_cast(args):
         e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
     if world > 1:
         dist.barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
