@@ -193,6 +193,32 @@ int launch_tc(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
 
 using namespace cast;
 
+// Scratch of cast_tree_attn_fwd_noalloc: one fixed array per device, part of
+// the library image, so that entry point never allocates. In host code this
+// name is only a stand-in for the symbol; the device address comes from
+// cudaGetSymbolAddress, looked up once per device by noalloc_scratch().
+static __device__ __align__(256) unsigned char g_noalloc_scratch[CAST_NOALLOC_SCRATCH_BYTES];
+
+namespace cast {
+namespace {
+std::atomic<void*> g_noalloc_ptr[kMaxDevices];
+
+// Device address of g_noalloc_scratch on the current device (nullptr on failure).
+void* noalloc_scratch() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  void* ptr = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (ptr) return ptr;
+  if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  g_noalloc_ptr[dev].store(ptr, std::memory_order_release);
+  return ptr;
+}
+}  // namespace
+}  // namespace cast
+
 extern "C" {
 
 const char* cast_strerror(int status) {
@@ -209,6 +235,7 @@ const char* cast_strerror(int status) {
     case CAST_ERR_LAUNCH: return "CUDA launch failed";
     case CAST_ERR_DEVICE: return "no usable CUDA device";
     case CAST_ERR_MASK_MODE: return "pass exactly one of anc_words and parent";
+    case CAST_ERR_SCRATCH_LIMIT: return "problem needs more scratch than the no-alloc entry point's fixed array (CAST_NOALLOC_SCRATCH_BYTES); use cast_tree_attn_fwd with a workspace";
     case CAST_DEV_BAD_LAYOUT: return "device: cu_q/cu_kv/prefix_len/pack_len out of range or above max_pack/max_kv";
     case CAST_DEV_BAD_PARENT: return "device: parent array is not a forest in pack order (need -1 <= parent[i] < i, parent[0] = -1)";
     case CAST_DEV_TIMEOUT: return "device: a bounded wait gave up";
@@ -328,6 +355,27 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
     case CAST_BF16: return launch_simt<__nv_bfloat16>(p, pl, st);
     default: return launch_simt<__half>(p, pl, st);
   }
+}
+
+int cast_tree_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* out, int dtype,
+                               const int64_t* strides,
+                               const int32_t* cu_q, const int32_t* cu_kv,
+                               const int32_t* prefix_len, const int32_t* pack_len,
+                               const int64_t* anc_words, int anc_words_per_row,
+                               const int32_t* parent,
+                               int B, int total_q, int total_kv, int H_q, int H_kv, int D,
+                               float sm_scale, int max_pack, int max_kv, cast_stream_t stream) {
+  // Same checks and launches as cast_tree_attn_fwd; only the scratch differs.
+  const size_t need = cast_tree_attn_workspace_size(dtype, B, total_q, H_q, H_kv, D, max_pack, max_kv);
+  if (need > (size_t)CAST_NOALLOC_SCRATCH_BYTES) return CAST_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if (need > 0) {
+    scratch = noalloc_scratch();
+    if (scratch == nullptr) return CAST_ERR_DEVICE;
+  }
+  return cast_tree_attn_fwd(q, k, v, out, dtype, strides, cu_q, cu_kv, prefix_len, pack_len, anc_words,
+                            anc_words_per_row, parent, B, total_q, total_kv, H_q, H_kv, D, sm_scale, max_pack,
+                            max_kv, scratch, need > 0 ? (size_t)CAST_NOALLOC_SCRATCH_BYTES : 0, stream);
 }
 
 int cast_block_topk(const double* logits, int64_t n_rows, int64_t V, int64_t row_stride, int k,

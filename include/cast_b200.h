@@ -51,6 +51,7 @@ enum cast_status {
   CAST_ERR_LAUNCH = -9,       /* the CUDA launch itself failed */
   CAST_ERR_DEVICE = -10,      /* no usable CUDA device */
   CAST_ERR_MASK_MODE = -11,   /* both or neither of anc_words / parent given */
+  CAST_ERR_SCRATCH_LIMIT = -12, /* cast_tree_attn_fwd_noalloc: problem needs more than CAST_NOALLOC_SCRATCH_BYTES */
   /* device-side codes (positive), reported by cast_device_error() */
   CAST_DEV_BAD_LAYOUT = 1,    /* cu/prefix/pack arrays out of range or above max_pack/max_kv */
   CAST_DEV_BAD_PARENT = 2,    /* parent[i] >= i or < -1 (or parent[0] != -1) */
@@ -109,6 +110,43 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
                        int B, int total_q, int total_kv, int H_q, int H_kv, int D,
                        float sm_scale, int max_pack, int max_kv,
                        void* workspace, size_t workspace_bytes, cast_stream_t stream);
+
+/*
+ * No counterpart in the reference: an added variant for callers that cannot
+ * allocate device memory.
+ *
+ * Same arguments, meaning and results as cast_tree_attn_fwd, minus the
+ * workspace: when the launch splits the key range, the fp32 partial results
+ * go to a fixed scratch array that the library itself holds in device memory
+ * (CAST_NOALLOC_SCRATCH_BYTES, reserved on every GPU that loads the library
+ * and kept until the process exits). It is meant for callers that are not
+ * allowed to call cudaMalloc or an allocator at this point: code running
+ * under a strict memory budget or a pre-reserved pool, plugin hosts that own
+ * all device allocations, or callers on a path where an allocation could
+ * block or fail. This call allocates nothing and calls no allocating routine.
+ *
+ * Limits and rules:
+ *   - Problems whose split partials need more than CAST_NOALLOC_SCRATCH_BYTES
+ *     (cast_tree_attn_workspace_size() above it) are rejected with
+ *     CAST_ERR_SCRATCH_LIMIT before anything is launched.
+ *   - The first call on each device looks up the scratch array's device
+ *     address (cudaGetSymbolAddress) with that device current; make that first
+ *     call before any stream capture begins.
+ *   - Every call on a device shares the one scratch array, which keeps the
+ *     last call's contents. Calls whose kernels may overlap on the GPU (other
+ *     streams, other host threads) race on it: issue them on one stream, or
+ *     order them with events. Nothing in it needs to start at zero: each call
+ *     writes every partial it later reads.
+ */
+#define CAST_NOALLOC_SCRATCH_BYTES (64u << 20) /* 64 MiB */
+int cast_tree_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* out, int dtype,
+                               const int64_t* strides,
+                               const int32_t* cu_q, const int32_t* cu_kv,
+                               const int32_t* prefix_len, const int32_t* pack_len,
+                               const int64_t* anc_words, int anc_words_per_row,
+                               const int32_t* parent,
+                               int B, int total_q, int total_kv, int H_q, int H_kv, int D,
+                               float sm_scale, int max_pack, int max_kv, cast_stream_t stream);
 
 /*
  * Bytes of workspace cast_tree_attn_fwd needs for these sizes (0 is possible).
