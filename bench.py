@@ -150,7 +150,7 @@ class Step:
         cb = self.cb
         cb.block_topk_device(self.logits, 8, self.idx, self.lp)
         trees = cb.build_trees(self.idx, self.lp, self.budget, 8, max_budget=N_NODES, cu_q=self.cu_q,
-                               root_token=self.roots, seq_len=self.seq_len)
+                               root_token=self.roots, seq_len=self.seq_len, total_q=self.lay["total_q"])
         if ev is not None:
             ev[0].record()
         self.out = cb.varlen_tree_attention(self.q, self.k, self.v, self.cu_q, self.cu_kv, self.prefix, self.pack,

@@ -35,7 +35,8 @@ def main():
     idx, lp = cast_b200.block_topk_device(logits, 8)
     t = lambda a: torch.from_numpy(a).to(dev)
     budget = torch.tensor(w.N, dtype=torch.int32, device=dev)
-    trees = cast_b200.build_trees(idx, lp, budget, 8, max_budget=max(w.N), cu_q=t(lay["cu_q"]))
+    cu_q = t(lay["cu_q"])
+    trees = cast_b200.build_trees(idx, lp, budget, 8, max_budget=max(w.N), cu_q=cu_q, total_q=lay["total_q"])
     q, k, v = w.make_qkv(dev)
     out = torch.empty_like(q)
     args_attn = (q, k, v, t(lay["cu_q"]), t(lay["cu_kv"]), t(lay["prefix_len"]), t(lay["pack_len"]), None)
@@ -47,7 +48,7 @@ def main():
         elif args.what == "topk":
             cast_b200.block_topk_device(logits, 8, idx, lp)
         else:
-            cast_b200.build_trees(idx, lp, budget, 8, max_budget=max(w.N), cu_q=t(lay["cu_q"]))
+            cast_b200.build_trees(idx, lp, budget, 8, max_budget=max(w.N), cu_q=cu_q, total_q=lay["total_q"])
 
     once()
     torch.cuda.synchronize()

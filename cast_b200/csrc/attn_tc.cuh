@@ -46,6 +46,10 @@ constexpr int SMEM_K = SMEM_Q + QT * TILE_BYTES;
 constexpr int SMEM_V = SMEM_K + NST * TILE_BYTES;
 constexpr int SMEM_ANC = SMEM_V + NST * TILE_BYTES;   // 196608
 constexpr float kRescaleLog2 = 8.0f;          // lazy O rescale threshold (factor 256)
+// Registers: launched at 168 per thread (384 x 168 = 64512, the whole file);
+// warpgroup 0 (TMA, MMA, two idle warps) gives back to 72, the two softmax
+// warpgroups take 216: 128 x 72 + 256 x 216 = 64512.
+constexpr int kRegsLow = 72, kRegsHigh = 216;
 
 __host__ __device__ inline int anc_tokens(int G) { return QT * BM / G + 2; }
 __host__ __device__ inline size_t smem_bytes(int G, int W) {
@@ -63,6 +67,26 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA pipe, to take part of the exponentials off the MUFU unit:
+// x = j + r with j = round(x) (the 1.5 * 2^23 shift leaves j in the low
+// mantissa bits) and r in [-1/2, 1/2]; 2^r by a degree-4 polynomial fitted here
+// by least squares on Chebyshev nodes of [-1/2, 1/2] (2.7e-6 relative, far
+// below the 16-bit rounding P gets next); 2^j added into the exponent field.
+// Arguments below -126 give about 2^-126 instead of 0, irrelevant next to a row
+// sum of at least 1; masked entries are zeroed by the caller.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const int j = __float_as_int(t) - 0x4B400000;
+  const float r = x - (t - 12582912.f);
+  float p = 0.009560510516166687f;
+  p = fmaf(p, r, 0.05591703951358795f);
+  p = fmaf(p, r, 0.24024981260299683f);
+  p = fmaf(p, r, 0.6931219696998596f);
+  p = fmaf(p, r, 0.9999991655349731f);
+  return __int_as_float(__float_as_int(p) + (j << 23));
 }
 
 template <bool BF16>
@@ -135,7 +159,8 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = tmem_base_sh;
-
+  if (warp < 4) {
+  regs_dec<kRegsLow>();
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -231,7 +256,9 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       }
       mma_commit(smem_u32(&bars.o_full));  // also on abort: tracks whatever was issued
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    regs_inc<kRegsHigh>();
     // ------------------------------------------------------------ softmax / epilogue
     const int q = (warp - 4) >> 2;
     const int t = tid - 128 - q * BM;  // == TMEM lane
@@ -249,10 +276,14 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       // Every tcgen05.ld/st below is .sync.aligned: control flow around them is
       // kept warp-uniform (waits are followed by a warp vote, per-row choices
       // are made with per-lane values inside uniform branches).
+      uint32_t sv[BN];
       for (int j = 0; j < n_kt; ++j) {
         ok = mbar_wait(smem_u32(&bars.s_full[q]), (uint32_t)j & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         fence_after_sync();
+        // the whole 128-column row of S in one round trip
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) tmem_ld32(S_t + cc * 32, sv + cc * 32);
         const int n0 = k_begin + j * BN;
         const bool full = (n0 + BN <= m.S) && (n0 + BN <= k_end);
         uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
@@ -273,50 +304,34 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
             vis[cc] = bits;
           }
         }
-        // pass 1: row max (raw scores; the scale c > 0 is applied once)
+        tmem_ld_wait();
+        // row max (raw scores; the scale c > 0 is applied once)
         float mx = -INFINITY;
+        if (full) {
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          tmem_ld32(S_t + cc * 32, v);
-          tmem_ld_wait();
-          if (full) {
+          for (int i = 0; i < BN; ++i) mx = fmaxf(mx, __uint_as_float(sv[i]));
+        } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) mx = ((vis[cc] >> i) & 1u) ? fmaxf(mx, __uint_as_float(v[i])) : mx;
-          }
+          for (int i = 0; i < BN; ++i) mx = ((vis[i >> 5] >> (i & 31)) & 1u) ? fmaxf(mx, __uint_as_float(sv[i])) : mx;
         }
         const float m_tile = (mx == -INFINITY) ? -INFINITY : mx * c;
         const bool grow = m_tile > m_ref + kRescaleLog2 || (m_ref == -INFINITY && m_tile != -INFINITY);
         const bool rescale = grow && m_ref != -INFINITY;
         const float alpha = rescale ? ex2(m_ref - m_tile) : 1.f;
         if (grow) m_ref = m_tile;
-        if (__any_sync(0xffffffffu, rescale)) {
-          l *= alpha;
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            tmem_ld32(O_t + cc * 32, v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-            tmem_st32(O_t + cc * 32, v);
-          }
-          tmem_st_wait();
-        }
         const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-        // pass 2: P = exp2(S*c - m), 16-bit, into the first 64 columns of S
+        // P = exp2(S*c - m) (3 of 4 on MUFU, 1 of 4 on the FMA pipe), 16-bit, into the first 64 columns of S
         float rs = 0.f;
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
-          tmem_ld32(S_t + cc * 32, v);
-          tmem_ld_wait();
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float s0 = __uint_as_float(v[2 * i]), s1 = __uint_as_float(v[2 * i + 1]);
-            float p0 = ex2(fmaf(s0, c, -m_use));
-            float p1 = ex2(fmaf(s1, c, -m_use));
+            const int e = cc * 32 + 2 * i;
+            const float x0 = fmaf(__uint_as_float(sv[e]), c, -m_use);
+            const float x1 = fmaf(__uint_as_float(sv[e + 1]), c, -m_use);
+            float p0 = ex2(x0);
+            float p1 = (i & 1) ? ex2_poly(x1) : ex2(x1);
             if (!full) {
               p0 = ((vis[cc] >> (2 * i)) & 1u) ? p0 : 0.f;
               p1 = ((vis[cc] >> (2 * i + 1)) & 1u) ? p1 : 0.f;
@@ -326,7 +341,18 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
           }
           tmem_st16(S_t + cc * 16, pk);
         }
-        l += rs;
+        l = l * alpha + rs;
+        // lazy correction of O (rows whose max grew by more than 2^8); PV_{j-1} is complete
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            tmem_ld32(O_t + cc * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            tmem_st32(O_t + cc * 32, v);
+          }
+        }
         tmem_st_wait();
         fence_before_sync();
         mbar_arrive(smem_u32(&bars.p_full[q]));

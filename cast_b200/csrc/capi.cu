@@ -387,13 +387,15 @@ int cast_block_topk(const double* logits, int64_t n_rows, int64_t V, int64_t row
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool vec = aligned(logits, 16) && (row_stride % 2 == 0);
   const dim3 grid((unsigned)n_rows);
+#define CAST_TOPK_LAUNCH(KC, VEC)                                                                        \
+  block_topk_kernel<KC, VEC><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);       \
+  block_topk_exact_kernel<KC, VEC><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);
   if (k <= 8) {
-    if (vec) block_topk_kernel<16, true><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);
-    else block_topk_kernel<16, false><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);
+    if (vec) { CAST_TOPK_LAUNCH(16, true) } else { CAST_TOPK_LAUNCH(16, false) }
   } else {
-    if (vec) block_topk_kernel<32, true><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);
-    else block_topk_kernel<32, false><<<grid, topk::NT, 0, st>>>(logits, V, row_stride, k, top_idx, top_lp);
+    if (vec) { CAST_TOPK_LAUNCH(32, true) } else { CAST_TOPK_LAUNCH(32, false) }
   }
+#undef CAST_TOPK_LAUNCH
   return cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
 }
 

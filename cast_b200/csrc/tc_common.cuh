@@ -86,6 +86,19 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
+// ---- register reallocation between warpgroups ------------------------------------
+// Executed by all 128 threads of a warpgroup. The block's register pool is
+// its launch allocation (threads x registers at launch): decreases by some
+// warpgroups must cover the increases of the others.
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---- tcgen05 ------------------------------------------------------------------
 // TMEM address: lane in bits 31..16, column in bits 15..0.
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {

@@ -9,23 +9,75 @@ namespace cast {
 // ---------------------------------------------------------------------------
 // block_topk (cast_trees/tree.py:20-26).
 //
-// One CTA per row of V logits. Pass 1 reads the row once; each thread keeps
-//  * an online (running max m_t, sum_t of exp(x - m_t)) pair, and
-//  * its KC best (x, index) candidates, sorted by x descending; a thread
-//    visits its elements in increasing index order, so an equal x never
-//    displaces an earlier one (the stable sort's lower-index-first rule).
-// The CTA merges both and forms lp = (x - M) - log(sum exp(x - M)), the
-// reference's operation order. The reference sorts on lp, and the rounding
-// of that subtraction can map distinct x to one lp; so the KC best by x are
-// re-sorted by (lp desc, index asc), which is exact whenever the k-th lp is
-// strictly above the KC-th (no element outside the candidates can then tie
-// into the top k). Otherwise - rows with many equal log-probs - pass 2 reads
-// the row again and selects the top k on lp itself, with M and the log-sum
-// of pass 1: exact in every case.
+// One CTA per row of V logits; the common case reads the row once. Each
+// thread keeps
+//  * the exact running max (the reference's x.max()),
+//  * sum_t = sum of exp(x - ref_t) against a reference ref_t that moves only
+//    when an element exceeds it by more than 2^8 nats worth of headroom (so
+//    the sum never overflows; fp64 keeps its relative precision at any scale),
+//  * its 4 best (x, index) candidates, sorted by x descending; a thread visits
+//    its elements in increasing index order, so an equal x never displaces an
+//    earlier one (the stable sort's lower-index-first rule).
+// The CTA merges the thread lists into its KC best by (x desc, index asc).
+// That set is exactly the row's KC best unless some thread's 4th candidate is
+// itself among them (the thread may have dropped a 5th): such rows take the
+// exact path below. With M the max and lse = log(sum exp(x - M)), the KC
+// candidates get lp = (x - M) - lse (the reference's operation order) and are
+// re-sorted by (lp desc, index asc); rounding in that subtraction can map
+// distinct x to one lp, so when the k-th and KC-th lp are equal an element
+// outside the candidates could tie into the top k, and the row also takes the
+// exact path: a second read that selects the top k on lp itself.
 // ---------------------------------------------------------------------------
 namespace topk {
 constexpr int NT = 256;
 constexpr int NW = NT / 32;
+constexpr int TL = 4;  // candidates per thread in the common path
+}
+
+// exp(t) in float64 for t <= 709, written from the mathematics: Cody-Waite
+// reduction t = k ln2 + r with ln 2 split into a 33-bit head (k * head exact
+// for |k| < 2^20) and its tail, |r| <= ln2/2, then the degree-12 Taylor
+// polynomial of e^r by Horner's rule (truncation < 2e-16 relative) and an
+// exponent-field scale by 2^k. Results below 2^-1022 are returned as 0: such
+// terms are more than 700 nats below the running reference and cannot move a
+// sum that includes a term of size 1.
+__device__ __forceinline__ double exp_fast(double t) {
+  constexpr double kLog2e = 1.4426950408889634;
+  constexpr double kLn2Hi = 0.6931471803691238;        // 0x1.62e42fee00000p-1
+  constexpr double kLn2Lo = 1.9082149292705877e-10;    // ln 2 - kLn2Hi
+  constexpr double kShift = 6755399441055744.0;        // 1.5 * 2^52: rounds to an integer in the low bits
+  const double kd = fma(t, kLog2e, kShift);
+  const int k = (int)(__double_as_longlong(kd) & 0xFFFFFFFFll);
+  const double kf = kd - kShift;
+  const double r = fma(-kf, kLn2Lo, fma(-kf, kLn2Hi, t));
+  double p = 2.08767569878681e-09;                    // 1/12!
+  p = fma(p, r, 2.505210838544172e-08);               // 1/11!
+  p = fma(p, r, 2.755731922398589e-07);               // 1/10!
+  p = fma(p, r, 2.7557319223985893e-06);              // 1/9!
+  p = fma(p, r, 2.48015873015873e-05);                // 1/8!
+  p = fma(p, r, 0.0001984126984126984);               // 1/7!
+  p = fma(p, r, 0.001388888888888889);                // 1/6!
+  p = fma(p, r, 0.008333333333333333);                // 1/5!
+  p = fma(p, r, 0.041666666666666664);                // 1/4!
+  p = fma(p, r, 0.16666666666666666);                 // 1/3!
+  p = fma(p, r, 0.5);
+  p = fma(p, r, 1.0);
+  p = fma(p, r, 1.0);
+  if (k < -1022) return 0.0;
+  return p * __longlong_as_double((long long)(k + 1023) << 52);
+}
+
+// Folds one element into a thread's (max, reference, sum of exp(x - reference)).
+__device__ __forceinline__ void lse_add(double& mx, double& ref, double& s, double v) {
+  mx = fmax(mx, v);
+  if (v == -INFINITY) return;
+  double t = v - ref;
+  if (!(t <= 256.0)) {
+    s = (ref == -INFINITY) ? 0.0 : s * exp_fast(ref - v);
+    ref = v;
+    t = 0.0;
+  }
+  s += exp_fast(t);
 }
 
 template <int KC>
@@ -37,9 +89,9 @@ struct CandList {
 #pragma unroll
     for (int i = 0; i < KC; ++i) { x[i] = -INFINITY; idx[i] = -1; }
   }
+  __device__ __forceinline__ bool wants(double v) const { return idx[KC - 1] < 0 || v > x[KC - 1]; }
   // j is larger than every index already held (increasing visit order).
-  __device__ __forceinline__ void offer(double v, int j) {
-    if (idx[KC - 1] >= 0 && !(v > x[KC - 1])) return;
+  __device__ __forceinline__ void insert(double v, int j) {
     x[KC - 1] = v;
     idx[KC - 1] = j;
 #pragma unroll
@@ -50,6 +102,9 @@ struct CandList {
         const int ti = idx[i]; idx[i] = idx[i - 1]; idx[i - 1] = ti;
       }
     }
+  }
+  __device__ __forceinline__ void offer(double v, int j) {
+    if (wants(v)) insert(v, j);
   }
   __device__ __forceinline__ void pop_front() {
 #pragma unroll
@@ -64,16 +119,6 @@ __device__ __forceinline__ bool cand_before(double ax, int ai, double bx, int bi
   if (ai < 0) return false;
   if (bi < 0) return true;
   return ax > bx || (ax == bx && ai < bi);
-}
-
-__device__ __forceinline__ void online_add(double& m, double& s, double v) {
-  if (v == -INFINITY) return;
-  if (v > m) {
-    s = s * exp(m - v) + 1.0;
-    m = v;
-  } else {
-    s += exp(v - m);
-  }
 }
 
 // Visits the row in each thread's increasing index order: f(value, index).
@@ -109,8 +154,8 @@ __device__ __forceinline__ void scan_row(const double* x, int64_t V, F&& f) {
 }
 
 // Merges every thread's sorted list into s_out_* (the CTA's KC best, best first).
-template <int KC>
-__device__ __forceinline__ void merge_lists(CandList<KC>& cl, double* s_cx, int* s_ci, double* s_out_x,
+template <int KC, int TLN>
+__device__ __forceinline__ void merge_lists(CandList<TLN>& cl, double* s_cx, int* s_ci, double* s_out_x,
                                             int* s_out_i) {
   using namespace topk;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -159,49 +204,51 @@ __global__ void __launch_bounds__(topk::NT)
 block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
                   int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
   using namespace topk;
-  __shared__ double s_m[NW], s_s[NW];
+  __shared__ double s_m[NW], s_r[NW], s_s[NW];
   __shared__ double s_cx[NW * KC];
   __shared__ int s_ci[NW * KC];
   __shared__ double s_fx[KC], s_flp[KC];
   __shared__ int s_fi[KC];
-  __shared__ double s_M, s_lse;
-  __shared__ int s_pass2;
-
   const int64_t row = blockIdx.x;
   const double* x = logits + row * row_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  CandList<KC> cl;
+  CandList<TL> cl;
   cl.init();
-  double m = -INFINITY, s = 0.0;
+  double mx = -INFINITY, ref = -INFINITY, s = 0.0;
   scan_row<VEC2>(x, V, [&](double v, int j) {
-    online_add(m, s, v);
-    cl.offer(v, j);
+    lse_add(mx, ref, s, v);
+    if (cl.wants(v)) cl.insert(v, j);
   });
+  const double my4x = cl.x[TL - 1];
+  const int my4i = cl.idx[TL - 1];
 
-  // (m, s): warp, then CTA
+  // (max, reference, sum): warp, then CTA
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
-    const double om = __shfl_xor_sync(0xffffffffu, m, off);
+    mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const double orf = __shfl_xor_sync(0xffffffffu, ref, off);
     const double os = __shfl_xor_sync(0xffffffffu, s, off);
-    const double mm = fmax(m, om);
-    if (mm != -INFINITY) {
-      s = (m == -INFINITY ? 0.0 : s * exp(m - mm)) + (om == -INFINITY ? 0.0 : os * exp(om - mm));
+    const double nr = fmax(ref, orf);
+    if (nr != -INFINITY) {
+      s = (ref == -INFINITY ? 0.0 : s * exp_fast(ref - nr)) + (orf == -INFINITY ? 0.0 : os * exp_fast(orf - nr));
     }
-    m = mm;
+    ref = nr;
   }
-  if (lane == 0) { s_m[warp] = m; s_s[warp] = s; }
-  merge_lists<KC>(cl, s_cx, s_ci, s_fx, s_fi);
+  if (lane == 0) { s_m[warp] = mx; s_r[warp] = ref; s_s[warp] = s; }
+  merge_lists<KC, TL>(cl, s_cx, s_ci, s_fx, s_fi);
+
+  // a thread whose 4th candidate made the CTA's KC best may have dropped a 5th
+  const bool saturated = my4i >= 0 && s_fi[KC - 1] >= 0 && !cand_before(s_fx[KC - 1], s_fi[KC - 1], my4x, my4i);
+  const int any_saturated = __syncthreads_or(saturated ? 1 : 0);
 
   if (tid == 0) {
     double M = s_m[0];
     for (int w = 1; w < NW; ++w) M = fmax(M, s_m[w]);
     double S = 0.0;
     for (int w = 0; w < NW; ++w)
-      if (s_m[w] != -INFINITY) S += s_s[w] * exp(s_m[w] - M);
+      if (s_r[w] != -INFINITY) S += s_s[w] * exp_fast(s_r[w] - M);
     const double lse = log(S);
-    s_M = M;
-    s_lse = lse;
     int n = 0;
     for (int c = 0; c < KC; ++c) {
       if (s_fi[c] < 0) break;
@@ -222,22 +269,64 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
       s_fi[c + 1] = iv;
     }
     const bool tie = V > KC && n == KC && s_flp[k - 1] == s_flp[KC - 1];
-    s_pass2 = tie ? 1 : 0;
-    if (!tie) {
+    if (tie || any_saturated) {
+      top_idx[row * k] = -1;  // hands the row to block_topk_exact_kernel
+    } else {
       for (int c = 0; c < k; ++c) {
         top_idx[row * k + c] = c < n ? (int64_t)s_fi[c] : (int64_t)0;
         top_lp[row * k + c] = c < n ? s_flp[c] : -INFINITY;
       }
     }
   }
-  __syncthreads();
-  if (!s_pass2) return;
+}
 
-  // pass 2: select on lp directly (rows whose boundary log-prob is tied)
+// Exact path of rows block_topk_kernel flagged (top_idx[row][0] == -1): one
+// read for the max and log-sum, a second that selects the k best on
+// lp = (x - M) - lse itself. Other rows exit at once.
+template <int KC, bool VEC2>
+__global__ void __launch_bounds__(topk::NT)
+block_topk_exact_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
+                        int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
+  using namespace topk;
+  __shared__ double s_m[NW], s_r[NW], s_s[NW];
+  __shared__ double s_cx[NW * KC];
+  __shared__ int s_ci[NW * KC];
+  __shared__ double s_flp[KC];
+  __shared__ int s_fi[KC];
+  __shared__ double s_M, s_lse;
+  const int64_t row = blockIdx.x;
+  if (top_idx[row * k] >= 0) return;
+  const double* x = logits + row * row_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  double mx = -INFINITY, ref = -INFINITY, s = 0.0;
+  scan_row<VEC2>(x, V, [&](double v, int) { lse_add(mx, ref, s, v); });
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const double orf = __shfl_xor_sync(0xffffffffu, ref, off);
+    const double os = __shfl_xor_sync(0xffffffffu, s, off);
+    const double nr = fmax(ref, orf);
+    if (nr != -INFINITY)
+      s = (ref == -INFINITY ? 0.0 : s * exp_fast(ref - nr)) + (orf == -INFINITY ? 0.0 : os * exp_fast(orf - nr));
+    ref = nr;
+  }
+  if (lane == 0) { s_m[warp] = mx; s_r[warp] = ref; s_s[warp] = s; }
+  __syncthreads();
+  if (tid == 0) {
+    double M = s_m[0];
+    for (int w = 1; w < NW; ++w) M = fmax(M, s_m[w]);
+    double S = 0.0;
+    for (int w = 0; w < NW; ++w)
+      if (s_r[w] != -INFINITY) S += s_s[w] * exp_fast(s_r[w] - M);
+    s_M = M;
+    s_lse = log(S);
+  }
+  __syncthreads();
   const double M = s_M, lse = s_lse;
-  cl.init();
-  scan_row<VEC2>(x, V, [&](double v, int j) { cl.offer((v - M) - lse, j); });
-  merge_lists<KC>(cl, s_cx, s_ci, s_flp, s_fi);
+  CandList<KC> full;
+  full.init();
+  scan_row<VEC2>(x, V, [&](double v, int j) { full.offer((v - M) - lse, j); });
+  merge_lists<KC, KC>(full, s_cx, s_ci, s_flp, s_fi);
   if (tid == 0) {
     for (int c = 0; c < k; ++c) {
       top_idx[row * k + c] = s_fi[c] >= 0 ? (int64_t)s_fi[c] : (int64_t)0;
@@ -294,6 +383,23 @@ __host__ __device__ inline size_t tree_smem_bytes(int max_budget, int L, int k) 
          (size_t)L * k * sizeof(double) + 64;                              // lp rows
 }
 
+// Warp-wide arg-min of a 128-bit key (hi, lo); every lane returns the winner's
+// slot (-1 if no lane has one). Four 32-bit redux.sync rounds, most
+// significant word first, then the one lane left holding the minimum.
+__device__ __forceinline__ int warp_argmin128(uint64_t hi, uint64_t lo, int slot) {
+  unsigned live = 0xffffffffu;
+  bool mine = slot >= 0;
+  const uint32_t w[4] = {(uint32_t)(hi >> 32), (uint32_t)hi, (uint32_t)(lo >> 32), (uint32_t)lo};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t m = __reduce_min_sync(0xffffffffu, mine ? w[i] : 0xffffffffu);
+    mine = mine && w[i] == m;
+  }
+  live = __ballot_sync(0xffffffffu, mine);
+  if (live == 0) return -1;
+  return __shfl_sync(0xffffffffu, slot, __ffs(live) - 1);
+}
+
 __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int b = blockIdx.x;
@@ -318,11 +424,21 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
   }
   const double* lp_g = a.top_lp + (size_t)b * L * a.k_cols;
   const int64_t* idx_g = a.top_idx + (size_t)b * L * a.k_cols;
-  for (int e = lane; e < L * k; e += 32) s_lp[e] = lp_g[(e / k) * a.k_cols + (e % k)];
+  bool sorted_rows = true;
+  for (int e = lane; e < L * k; e += 32) {
+    const double v = lp_g[(e / k) * a.k_cols + (e % k)];
+    s_lp[e] = v;
+    if (e % k != k - 1 && !(v >= lp_g[(e / k) * a.k_cols + (e % k) + 1])) sorted_rows = false;
+  }
+  // Rows sorted best-first (block_topk's output): fl(neg - lp[d, r]) is then
+  // non-decreasing in r, so every node's children leave the heap in rank
+  // order and the sibling order needs no sorting.
+  sorted_rows = __all_sync(0xffffffffu, sorted_rows);
   __syncwarp();
 
   // child order of a node whose own neg is `base` (root: children neg = -lp[0, r])
   auto child_order = [&](int slot, bool root, double base, int d) {
+    if (sorted_rows) return;
     uint64_t hi = ~0ull;
     if (lane < k) hi = ordered_key(root ? -s_lp[lane] : base - s_lp[d * k + lane]);
     int rank = 0;
@@ -333,12 +449,13 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
     if (lane < k) order[(size_t)slot * k + rank] = (unsigned char)lane;
     __syncwarp();
   };
+  auto nth_child = [&](int slot, int j) -> int { return sorted_rows ? j : (int)order[(size_t)slot * k + j]; };
 
   int ncand = 0;
   if (budget > 0 && k > 0 && L > 0) {
     child_order(0, true, 0.0, 0);
     if (lane == 0) {
-      const int r = order[0];
+      const int r = nth_child(0, 0);
       const double neg = -s_lp[r];
       c_hi[0] = ordered_key(neg);
       c_lo[0] = (1ull << 40) | (0ull << 8) | (uint64_t)r;
@@ -358,21 +475,14 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
   pack_ok = __shfl_sync(0xffffffffu, pack_ok ? 1 : 0, 0) != 0;
 
   while (n < budget && ncand > 0) {
-    // arg-min over the candidate set
+    // arg-min over the candidate set: a scan of this lane's slots, then the warp
     uint64_t bh = ~0ull, bl = ~0ull;
     int bs = -1;
     for (int c = lane; c < ncand; c += 32) {
       const uint64_t h = c_hi[c], l = c_lo[c];
       if (bs < 0 || h < bh || (h == bh && l < bl)) { bh = h; bl = l; bs = c; }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const uint64_t oh = __shfl_xor_sync(0xffffffffu, bh, off);
-      const uint64_t ol = __shfl_xor_sync(0xffffffffu, bl, off);
-      const int os = __shfl_xor_sync(0xffffffffu, bs, off);
-      if (os >= 0 && (bs < 0 || oh < bh || (oh == bh && ol < bl))) { bh = oh; bl = ol; bs = os; }
-    }
-    const int slot = bs;
+    const int slot = warp_argmin128(bh, bl, bs);
     const double neg = c_neg[slot];
     const int par = c_par[slot], j = c_j[slot], d = c_d[slot], r = c_r[slot];
     const int me = n;
@@ -392,7 +502,7 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
       }
       // the popped slot takes the next sibling, or the last candidate
       if (j + 1 < k) {
-        const int r2 = order[(size_t)(par + 1) * k + j + 1];
+        const int r2 = nth_child(par + 1, j + 1);
         const double sneg = (par < 0) ? -s_lp[r2] : n_neg[par] - s_lp[(size_t)(d - 1) * k + r2];
         c_hi[slot] = ordered_key(sneg);
         c_lo[slot] = ((uint64_t)d << 40) | ((uint64_t)(par + 1) << 8) | (uint64_t)r2;
@@ -408,7 +518,7 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
     if (d < L) {
       child_order(me + 1, false, neg, d);
       if (lane == 0) {
-        const int r2 = order[(size_t)(me + 1) * k];
+        const int r2 = nth_child(me + 1, 0);
         const double cneg = neg - s_lp[(size_t)d * k + r2];
         const int c = ncand;
         c_hi[c] = ordered_key(cneg);

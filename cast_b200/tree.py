@@ -85,13 +85,14 @@ def block_topk(logits, k=8):
 
 
 def build_trees(top_idx, top_lp, budget, k=8, *, max_budget=None, cu_q=None, root_token=None,
-                seq_len=None):
+                seq_len=None, total_q=None):
     """Batched best-first trees on the device.
 
     top_idx int64 [B, L, kc], top_lp float64 [B, L, kc] (CUDA); budget: int or
     int32 [B]. With cu_q (int32 [B+1]) the pack-local parent array of each
     pack is written at its rows; root_token / seq_len add the packed tokens
-    and positions.
+    and positions. Pass total_q (= cu_q[-1]) and, for a tensor budget,
+    max_budget to keep the call free of device-to-host reads.
     """
     dev = top_idx.device
     B, L, kc = top_idx.shape
@@ -112,7 +113,8 @@ def build_trees(top_idx, top_lp, budget, k=8, *, max_budget=None, cu_q=None, roo
     cu_ptr = rt_ptr = sl_ptr = None
     if cu_q is not None:
         cu_q = torch.as_tensor(cu_q, device=dev).to(torch.int32).contiguous()
-        total_q = int(cu_q[-1].item())
+        if total_q is None:
+            total_q = int(cu_q[-1].item())
         cu_ptr = cu_q.data_ptr()
         pack_parent = torch.empty(total_q, dtype=torch.int32, device=dev)
         if root_token is not None:
