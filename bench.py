@@ -1,10 +1,14 @@
 """Benchmark of the ragged tree-verification hot path on B200.
 
-One step = one verify pass over a batch: GPU block_topk of the drafter's
-fp64 block scores, GPU best-first tree build (pack parents written in the
-same launch), then one ragged tree-attention call consuming those parents.
-Workload at N=1: BASELINE configuration 3 (B=64, N=127, prefix ~ U[4096,8192],
-Llama-3.1-8B attention geometry 32/8 heads, d=128, bf16, V=128256), synthetic.
+One step = one verify round over a batch, as CAST runs it: GPU block_topk of
+the drafter's fp64 block scores and GPU best-first tree build (pack parents
+written in the same launch) once per round, then one ragged tree-attention
+call per decoder layer consuming those parents (cast_trees/serving.py calls
+its attention hook once per layer of the target forward). Workload at N=1:
+BASELINE configuration 3 (B=64, N=127, prefix ~ U[4096,8192], Llama-3.1-8B
+attention geometry 32/8 heads, d=128, 32 layers, bf16, V=128256), synthetic;
+the layers share one synthetic K/V set (1.59 GB, far larger than L2, so each
+call streams it from HBM).
 With --gpus N (one process per GPU under torchrun) every rank runs its own
 64 sequences of the same recipe (weak scaling, no collective on the path).
 
@@ -145,17 +149,19 @@ class Step:
         self.lp = torch.empty((w.B, 15, 8), dtype=torch.float64, device=dev)
         self.ws = None
 
-    def run(self, ev=None):
-        """ev: optional (start, mid, end) events around the attention call."""
+    def run(self, layers, ev=None):
+        """One verify round; ev: optional (start, end) events around the attention calls."""
         cb = self.cb
         cb.block_topk_device(self.logits, 8, self.idx, self.lp)
         trees = cb.build_trees(self.idx, self.lp, self.budget, 8, max_budget=N_NODES, cu_q=self.cu_q,
                                root_token=self.roots, seq_len=self.seq_len, total_q=self.lay["total_q"])
         if ev is not None:
             ev[0].record()
-        self.out = cb.varlen_tree_attention(self.q, self.k, self.v, self.cu_q, self.cu_kv, self.prefix, self.pack,
-                                            None, parent=trees.pack_parent, max_pack=self.lay["max_pack"],
-                                            max_kv=self.lay["max_kv"], out=self.out, workspace=self.ws)
+        for _ in range(layers):
+            self.out = cb.varlen_tree_attention(self.q, self.k, self.v, self.cu_q, self.cu_kv, self.prefix,
+                                                self.pack, None, parent=trees.pack_parent,
+                                                max_pack=self.lay["max_pack"], max_kv=self.lay["max_kv"],
+                                                out=self.out, workspace=self.ws)
         if ev is not None:
             ev[1].record()
         return trees
@@ -189,17 +195,18 @@ def run_cast(args):
     # launches per step: block_topk + build_tree + attention (+ combine when the keys are split)
     kernel, n_split, attn_launches = cast_b200.attention_plan(st.q, st.k, st.v, st.out, w.B, w.layout()["max_pack"],
                                                               w.layout()["max_kv"])
-    launches_per_step = 2 + attn_launches
+    launches_per_step = 3 + attn_launches * args.layers   # topk (fast + exact kernels), tree, attention
 
     for _ in range(args.warmup):
-        trees = st.run()
+        trees = st.run(args.layers)
     torch.cuda.synchronize()
     err = _lib.device_error()
     if err != 0:
         raise RuntimeError(f"device error {err} after warm-up")
     depth_sums = trees.depth.sum(dim=1, dtype=torch.int64).cpu().tolist()
-    flops = w.attn_flops(depth_sums)
-    attn_bytes = w.attn_bytes()
+    call_flops = w.attn_flops(depth_sums)
+    call_bytes = w.attn_bytes()
+    flops = call_flops * args.layers          # per step
 
     stream = torch.cuda.current_stream()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -211,14 +218,14 @@ def run_cast(args):
     torch.cuda.synchronize()
     t0.record(stream)
     for i in range(args.steps):
-        st.run(evs[i])
+        st.run(args.layers, evs[i])
     t1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     step_ms = t0.elapsed_time(t1) / args.steps
-    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    tree_ms = step_ms - attn_ms
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in evs) / args.layers   # per call
+    tree_ms = step_ms - attn_ms * args.layers
 
     # e2e: the public API with host buffers, copies inside the timed region
     h2d = sum(x.numel() * x.element_size() for x in (h_logits, h_q, h_k, h_v))
@@ -229,7 +236,7 @@ def run_cast(args):
         st.q.copy_(h_q, non_blocking=True)
         st.k.copy_(h_k, non_blocking=True)
         st.v.copy_(h_v, non_blocking=True)
-        st.run()
+        st.run(args.layers)
         h_out.copy_(st.out, non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
@@ -250,7 +257,7 @@ def run_cast(args):
 
     # max over ranks of every time; sums of work
     t = torch.tensor([step_ms, attn_ms, tree_ms, e2e_ms], dtype=torch.float64, device=dev)
-    work = torch.tensor([flops, attn_bytes], dtype=torch.float64, device=dev)
+    work = torch.tensor([flops, call_bytes], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.all_reduce(work, op=dist.ReduceOp.SUM)
@@ -259,12 +266,12 @@ def run_cast(args):
     hbm, tf_burst, tf_sus, peak_kind = _peaks()
 
     value = tot_flops / (step_ms * 1e-3) / 1e12
-    attn_tflops = flops / (attn_ms * 1e-3) / 1e12          # per GPU, dominant kernel
-    attn_gbs = attn_bytes / (attn_ms * 1e-3) / 1e9
+    attn_tflops = call_flops / (attn_ms * 1e-3) / 1e12     # per GPU, dominant kernel, per call
+    attn_gbs = call_bytes / (attn_ms * 1e-3) / 1e9
     topk_gbs = w.topk_bytes() / (tree_ms * 1e-3) / 1e9
     # binding roofline of the attention kernel: the slower of the HBM and tensor floors
-    t_hbm = attn_bytes / (hbm * 1e9)
-    t_tensor = flops / (tf_burst * 1e12)
+    t_hbm = call_bytes / (hbm * 1e9)
+    t_tensor = call_flops / (tf_burst * 1e12)
     bound = "tensor" if t_tensor >= t_hbm else "hbm"
     if bound == "tensor":
         roof = {"bound": "tensor", "achieved": round(attn_tflops, 2), "peak": tf_burst, "unit": "TFLOP/s",
@@ -282,8 +289,9 @@ def run_cast(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded normal(scale=5) block scores 15x128256 fp64, q/k/v N(0,1)*0.5 bf16",
-        "config": {"workload": "config3: B=64/GPU, N=127 (P=128), prefix U[4096,8192], 32/8 heads, d=128, "
-                               "V=128256; step = block_topk + build_tree + tree attention",
+        "config": {"workload": f"config3: B=64/GPU, N=127 (P=128), prefix U[4096,8192], 32/8 heads, d=128, "
+                               f"V=128256; step = one verify round: block_topk + build_tree + {args.layers} "
+                               f"tree-attention calls (one per layer)", "layers": args.layers,
                    "global_batch": B_PER_RANK * world, "seq_len": "4096-8192 (ragged)",
                    "parallelism": f"sequence-sharded x{world}, no collective",
                    "l2": "inputs larger than L2 (logits 0.98 GB + K/V 1.59 GB streamed per step)"},
@@ -311,8 +319,9 @@ def run_cast(args):
 def _cpu_sample(w, ids):
     """Times the oracle (the reference's CPU algorithms) on sequences `ids` of w.
 
-    Returns (seconds, flops, trees); q/k/v come from the same generator as the
-    GPU arm (drawn on the CPU here).
+    Returns (tree_seconds, attention_seconds_per_call, flops_per_call, trees):
+    numpy block_topk + heap build_tree once, then one fp32 masked-softmax
+    attention call (torch, all threads). q/k/v are drawn on the CPU.
     """
     from oracle import attn as oattn
     from oracle import tree as otree
@@ -330,17 +339,19 @@ def _cpu_sample(w, ids):
         tr = otree.build_tree(idx, lp, sub.N[b])
         trees.append(tr)
         words.append(otree.ancestor_words(otree.pack_parent(tr.parent)))
+    t1 = time.perf_counter()
     oattn.tree_attention(q.float(), k.float(), v.float(), lay["cu_q"], lay["cu_kv"], lay["prefix_len"],
                          lay["pack_len"], words)
-    dt = time.perf_counter() - t0
+    t2 = time.perf_counter()
     flops = sub.attn_flops([int(t.depth.sum()) for t in trees])
-    return dt, flops, trees
+    return t1 - t0, t2 - t1, flops, trees
 
 
 def cpu_baseline(w, trees_gpu, args):
     n = max(1, args.cpu_seqs)
     torch.set_num_threads(os.cpu_count() or 1)
-    dt, flops, trees = _cpu_sample(w, list(range(n)))
+    t_tree, t_attn, flops, trees = _cpu_sample(w, list(range(n)))
+    round_s = t_tree + args.layers * t_attn
     exact = True
     for b in range(n):
         c = int(trees_gpu.count[b])
@@ -348,11 +359,12 @@ def cpu_baseline(w, trees_gpu, args):
         exact &= np.array_equal(trees_gpu.parent[b, :c].cpu().numpy(), trees[b].parent)
         exact &= np.array_equal(trees_gpu.token[b, :c].cpu().numpy(), trees[b].token)
         exact &= np.array_equal(trees_gpu.depth[b, :c].cpu().numpy(), trees[b].depth)
-    return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-            "kind": "port",
-            "sample": f"{n} of the {w.B} config-3 sequences: numpy block_topk + heap build_tree (1 thread) "
-                      f"and fp32 masked-softmax attention (torch, all threads); {dt:.2f} s",
-            "seconds": round(dt, 3), "tree_arrays_bit_exact_vs_gpu": bool(exact)}
+    return {"value": round(args.layers * flops / round_s / 1e12, 6), "unit": "TFLOP/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} of the {w.B} config-3 sequences: numpy block_topk + heap build_tree once "
+                      f"({t_tree:.2f} s, 1 thread) and one fp32 masked-softmax attention call "
+                      f"({t_attn:.3f} s, torch, all threads) counted {args.layers}x (one per layer)",
+            "tree_arrays_bit_exact_vs_gpu": bool(exact)}
 
 
 def run_reference(args):
@@ -365,10 +377,10 @@ def run_reference(args):
     times, flops = [], 0
     for i in range(args.warmup + args.steps):
         ids = [(i * n + j) % w.B for j in range(n)]
-        dt, fl, _ = _cpu_sample(w, ids)
+        t_tree, t_attn, fl, _ = _cpu_sample(w, ids)
         if i >= args.warmup:
-            times.append(dt)
-            flops += fl
+            times.append(t_tree + args.layers * t_attn)
+            flops += fl * args.layers
     tot = sum(times)
     value = flops / tot / 1e12
     print(json.dumps({
@@ -376,10 +388,13 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * tot / args.steps, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 inputs, fp32 compute",
         "data": "synthetic (config-3 recipe)",
-        "config": {"workload": f"config3 sample: {n} sequences per step (block_topk + build_tree + attention)",
-                   "global_batch": n, "seq_len": "4096-8192 (ragged)", "parallelism": "host CPU"},
+        "config": {"workload": f"config3 sample: {n} sequences per step, one verify round (block_topk + "
+                               f"build_tree once, attention counted once per layer, {args.layers} layers)",
+                   "global_batch": n, "seq_len": "4096-8192 (ragged)", "parallelism": "host CPU",
+                   "layers": args.layers},
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": f"{n} config-3 sequences per step"},
+                         "kind": "port", "sample": f"{n} config-3 sequences per step; the reference is Python: "
+                                                   f"its numpy tree builder and its fp32 masked-softmax attention"},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -390,7 +405,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["cast", "reference"], default="cast")
-    ap.add_argument("--cpu-seqs", type=int, default=16, help="sequences in the cpu_baseline sample")
+    ap.add_argument("--layers", type=int, default=32, help="attention calls per verify round (decoder layers)")
+    ap.add_argument("--cpu-seqs", type=int, default=8, help="sequences in the cpu_baseline sample")
     ap.add_argument("--ref-seqs", type=int, default=2, help="sequences per step of --impl reference")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -47,9 +47,9 @@ constexpr int SMEM_V = SMEM_K + NST * TILE_BYTES;
 constexpr int SMEM_ANC = SMEM_V + NST * TILE_BYTES;   // 196608
 constexpr float kRescaleLog2 = 8.0f;          // lazy O rescale threshold (factor 256)
 // Registers: launched at 168 per thread (384 x 168 = 64512, the whole file);
-// warpgroup 0 (TMA, MMA, two idle warps) gives back to 72, the two softmax
-// warpgroups take 216: 128 x 72 + 256 x 216 = 64512.
-constexpr int kRegsLow = 72, kRegsHigh = 216;
+// warpgroup 0 (TMA, MMA, two idle warps) gives back to 80, the two softmax
+// warpgroups take 208: 128 x 80 + 256 x 208 = 63488 <= 64512.
+constexpr int kRegsLow = 80, kRegsHigh = 208;
 
 __host__ __device__ inline int anc_tokens(int G) { return QT * BM / G + 2; }
 __host__ __device__ inline size_t smem_bytes(int G, int W) {
@@ -305,15 +305,20 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
           }
         }
         tmem_ld_wait();
-        // row max (raw scores; the scale c > 0 is applied once)
-        float mx = -INFINITY;
+        // row max (raw scores; the scale c > 0 is applied once), 8 independent chains
+        float mm[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mm[a] = -INFINITY;
         if (full) {
 #pragma unroll
-          for (int i = 0; i < BN; ++i) mx = fmaxf(mx, __uint_as_float(sv[i]));
+          for (int i = 0; i < BN; ++i) mm[i & 7] = fmaxf(mm[i & 7], __uint_as_float(sv[i]));
         } else {
 #pragma unroll
-          for (int i = 0; i < BN; ++i) mx = ((vis[i >> 5] >> (i & 31)) & 1u) ? fmaxf(mx, __uint_as_float(sv[i])) : mx;
+          for (int i = 0; i < BN; ++i)
+            mm[i & 7] = ((vis[i >> 5] >> (i & 31)) & 1u) ? fmaxf(mm[i & 7], __uint_as_float(sv[i])) : mm[i & 7];
         }
+        const float mx = fmaxf(fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3])),
+                               fmaxf(fmaxf(mm[4], mm[5]), fmaxf(mm[6], mm[7])));
         const float m_tile = (mx == -INFINITY) ? -INFINITY : mx * c;
         const bool grow = m_tile > m_ref + kRescaleLog2 || (m_ref == -INFINITY && m_tile != -INFINITY);
         const bool rescale = grow && m_ref != -INFINITY;
@@ -321,7 +326,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
         if (grow) m_ref = m_tile;
         const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
         // P = exp2(S*c - m) (3 of 4 on MUFU, 1 of 4 on the FMA pipe), 16-bit, into the first 64 columns of S
-        float rs = 0.f;
+        float rsum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           uint32_t pk[16];
@@ -336,12 +341,12 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
               p0 = ((vis[cc] >> (2 * i)) & 1u) ? p0 : 0.f;
               p1 = ((vis[cc] >> (2 * i + 1)) & 1u) ? p1 : 0.f;
             }
-            rs += p0 + p1;
+            rsum[i & 3] += p0 + p1;
             pk[i] = pack2<BF16>(p0, p1);
           }
           tmem_st16(S_t + cc * 16, pk);
         }
-        l = l * alpha + rs;
+        l = l * alpha + ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3]));
         // lazy correction of O (rows whose max grew by more than 2^8); PV_{j-1} is complete
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
