@@ -12,7 +12,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
-LIB_PATH = PKG / "libcast_b200.so"
+LIB_PATH = Path(os.environ["CAST_B200_LIB"]) if os.environ.get("CAST_B200_LIB") else PKG / "libcast_b200.so"
 HEADER = ROOT / "include" / "cast_b200.h"
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -37,6 +37,8 @@ def _sources():
 
 
 def needs_build():
+    if os.environ.get("CAST_B200_LIB"):
+        return False          # an explicitly chosen build is used as it is
     if not LIB_PATH.exists():
         return True
     t = LIB_PATH.stat().st_mtime

@@ -47,9 +47,9 @@ constexpr int SMEM_V = SMEM_K + NST * TILE_BYTES;
 constexpr int SMEM_ANC = SMEM_V + NST * TILE_BYTES;   // 196608
 constexpr float kRescaleLog2 = 8.0f;          // lazy O rescale threshold (factor 256)
 // Registers: launched at 168 per thread (384 x 168 = 64512, the whole file);
-// warpgroup 0 (TMA, MMA, two idle warps) gives back to 80, the two softmax
-// warpgroups take 208: 128 x 80 + 256 x 208 = 63488 <= 64512.
-constexpr int kRegsLow = 80, kRegsHigh = 208;
+// warpgroup 0 (TMA, MMA, two idle warps) gives back to 104, the two softmax
+// warpgroups take 200: 128 x 104 + 256 x 200 = 64512.
+constexpr int kRegsLow = 104, kRegsHigh = 200;
 
 __host__ __device__ inline int anc_tokens(int G) { return QT * BM / G + 2; }
 __host__ __device__ inline size_t smem_bytes(int G, int W) {
@@ -69,24 +69,10 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, to take part of the exponentials off the MUFU unit:
-// x = j + r with j = round(x) (the 1.5 * 2^23 shift leaves j in the low
-// mantissa bits) and r in [-1/2, 1/2]; 2^r by a degree-4 polynomial fitted here
-// by least squares on Chebyshev nodes of [-1/2, 1/2] (2.7e-6 relative, far
-// below the 16-bit rounding P gets next); 2^j added into the exponent field.
-// Arguments below -126 give about 2^-126 instead of 0, irrelevant next to a row
-// sum of at least 1; masked entries are zeroed by the caller.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;
-  const int j = __float_as_int(t) - 0x4B400000;
-  const float r = x - (t - 12582912.f);
-  float p = 0.009560510516166687f;
-  p = fmaf(p, r, 0.05591703951358795f);
-  p = fmaf(p, r, 0.24024981260299683f);
-  p = fmaf(p, r, 0.6931219696998596f);
-  p = fmaf(p, r, 0.9999991655349731f);
-  return __int_as_float(__float_as_int(p) + (j << 23));
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 template <bool BF16>
@@ -161,101 +147,126 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   const uint32_t tmem = tmem_base_sh;
   if (warp < 4) {
   regs_dec<kRegsLow>();
+  // Warps 0 and 1 walk their schedules converged, so warp-uniform values (loop
+  // counters, shared-memory addresses, descriptors) stay in uniform registers;
+  // one elected lane issues each TMA copy / MMA / commit.
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      const uint32_t qf = smem_u32(&bars.q_full);
+    const uint32_t qf = smem_u32(&bars.q_full);
+    if (elect_one()) {
       mbar_expect_tx(qf, n_qt * TILE_BYTES);
       for (int q = 0; q < n_qt; ++q) {
         const int tok = m.q0 + (r_base + q * BM) / G;
         for (int hf = 0; hf < 2; ++hf)
           tma_load_3d(smem_u32(smem + SMEM_Q + q * TILE_BYTES + hf * HALF_BYTES), &tmQ, hf * 64, h * G, tok, qf);
       }
-      int issued = 0;
-      for (int j = 0; j < n_kt; ++j) {
-        const int s = j % NST;
-        const uint32_t use = (uint32_t)(j / NST);
-        const int row = m.kv0 + k_begin + j * BN;
-        if (j >= NST && !mbar_wait(smem_u32(&bars.k_empty[s]), (use - 1) & 1, abort_flag)) break;
+    }
+    __syncwarp();
+    int issued = 0;
+    for (int j = 0; j < n_kt; ++j) {
+      const int s = j % NST;
+      const uint32_t use = (uint32_t)(j / NST);
+      const int row = m.kv0 + k_begin + j * BN;
+      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.k_empty[s]), (use - 1) & 1, abort_flag)))
+        break;
+      if (elect_one()) {
         mbar_expect_tx(smem_u32(&bars.k_full[s]), TILE_BYTES);
         for (int hf = 0; hf < 2; ++hf)
           tma_load_3d(smem_u32(smem + SMEM_K + s * TILE_BYTES + hf * HALF_BYTES), &tmK, hf * 64, h, row,
                       smem_u32(&bars.k_full[s]));
-        if (j >= NST && !mbar_wait(smem_u32(&bars.v_empty[s]), (use - 1) & 1, abort_flag)) {
-          issued = j + 1;  // K of tile j is in flight
-          break;
-        }
+      }
+      __syncwarp();
+      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.v_empty[s]), (use - 1) & 1, abort_flag))) {
+        issued = j + 1;  // K of tile j is in flight
+        break;
+      }
+      if (elect_one()) {
         mbar_expect_tx(smem_u32(&bars.v_full[s]), TILE_BYTES);
         for (int hf = 0; hf < 2; ++hf)
           tma_load_3d(smem_u32(smem + SMEM_V + s * TILE_BYTES + hf * HALF_BYTES), &tmV, hf * 64, h, row,
                       smem_u32(&bars.v_full[s]));
-        issued = j + 1;
       }
-      // let the last copies land before the CTA can exit (immediate on the normal path)
-      for (int j = max(0, issued - NST); j < issued; ++j) {
-        const int s = j % NST;
-        const uint32_t ph = (uint32_t)(j / NST) & 1;
-        mbar_wait(smem_u32(&bars.k_full[s]), ph, nullptr);
-        mbar_wait(smem_u32(&bars.v_full[s]), ph, nullptr);
-      }
-      mbar_wait(qf, 0, nullptr);
+      __syncwarp();
+      issued = j + 1;
     }
+    // let the last copies land before the CTA can exit (immediate on the normal path)
+    for (int j = max(0, issued - NST); j < issued; ++j) {
+      const int s = j % NST;
+      const uint32_t ph = (uint32_t)(j / NST) & 1;
+      mbar_wait(smem_u32(&bars.k_full[s]), ph, nullptr);
+      mbar_wait(smem_u32(&bars.v_full[s]), ph, nullptr);
+    }
+    mbar_wait(qf, 0, nullptr);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false, false);
-      constexpr uint32_t idesc_pv = idesc_f16(BF16, BM, D, false, true);
-      const uint32_t sQ = smem_u32(smem + SMEM_Q), sK = smem_u32(smem + SMEM_K), sV = smem_u32(smem + SMEM_V);
-      auto qk = [&](int q, int j) {
-        const uint32_t a0 = sQ + q * TILE_BYTES, b0 = sK + (j % NST) * TILE_BYTES;
+    constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false, false);
+    constexpr uint32_t idesc_pv = idesc_f16(BF16, BM, D, false, true);
+    const uint32_t sQ = smem_u32(smem + SMEM_Q), sK = smem_u32(smem + SMEM_K), sV = smem_u32(smem + SMEM_V);
+    // descriptors of every tile base; a K step adds its byte offset / 16 to the start-address field
+    const uint64_t dQ0 = desc_kmajor(sQ), dQ1 = desc_kmajor(sQ + TILE_BYTES);
+    const uint64_t dK0 = desc_kmajor(sK), dK1 = desc_kmajor(sK + TILE_BYTES);
+    const uint64_t dV0 = desc_mnmajor(sV, HALF_BYTES), dV1 = desc_mnmajor(sV + TILE_BYTES, HALF_BYTES);
+    auto qk = [&](int q, int j) {
+      const uint64_t a = q ? dQ1 : dQ0, b = (j % NST) ? dK1 : dK0;
+      if (elect_one()) {
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * HALF_BYTES + (k & 3) * 32;
-          mma_ss(tmem + q * 128, desc_kmajor(a0 + off), desc_kmajor(b0 + off), idesc_qk, k > 0 ? 1u : 0u);
+          const uint64_t off = (uint64_t)(((k >> 2) * HALF_BYTES + (k & 3) * 32) >> 4);
+          mma_ss(tmem + q * 128, a + off, b + off, idesc_qk, k > 0 ? 1u : 0u);
         }
-      };
-      auto pv = [&](int q, int j) {
-        const uint32_t b0 = sV + (j % NST) * TILE_BYTES;
+      }
+      __syncwarp();
+    };
+    auto pv = [&](int q, int j) {
+      const uint64_t b = (j % NST) ? dV1 : dV0;
+      if (elect_one()) {
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k)
-          mma_ts(tmem + 256 + q * 128, tmem + q * 128 + k * 8, desc_mnmajor(b0 + k * 2048, HALF_BYTES), idesc_pv,
+          mma_ts(tmem + 256 + q * 128, tmem + q * 128 + k * 8, b + (uint64_t)((k * 2048) >> 4), idesc_pv,
                  (j > 0 || k > 0) ? 1u : 0u);
-      };
-      bool ok = mbar_wait(smem_u32(&bars.q_full), 0, abort_flag);
-      int j = 0;
-      for (; ok && j < n_kt; ++j) {
-        const int s = j % NST;
-        const uint32_t ph = (uint32_t)(j / NST) & 1;
-        if (!(ok = mbar_wait(smem_u32(&bars.k_full[s]), ph, abort_flag))) break;
-        fence_after_sync();
-        qk(0, j);
-        mma_commit(smem_u32(&bars.s_full[0]));
-        if (n_qt == 2) {
-          if (j > 0) {
-            if (!(ok = mbar_wait(smem_u32(&bars.p_full[1]), (uint32_t)(j - 1) & 1, abort_flag))) break;
-            fence_after_sync();
-            pv(1, j - 1);
-            mma_commit(smem_u32(&bars.v_empty[(j - 1) % NST]));
-          }
-          qk(1, j);
-          mma_commit(smem_u32(&bars.s_full[1]));
-        }
-        mma_commit(smem_u32(&bars.k_empty[s]));
-        if (!(ok = mbar_wait(smem_u32(&bars.v_full[s]), ph, abort_flag))) break;
-        if (!(ok = mbar_wait(smem_u32(&bars.p_full[0]), (uint32_t)j & 1, abort_flag))) break;
-        fence_after_sync();
-        pv(0, j);
-        if (n_qt == 1) mma_commit(smem_u32(&bars.v_empty[s]));
       }
-      if (ok && n_qt == 2) {
-        if (mbar_wait(smem_u32(&bars.p_full[1]), (uint32_t)(n_kt - 1) & 1, abort_flag)) {
+      __syncwarp();
+    };
+    auto commit = [&](uint64_t& bar) {
+      if (elect_one()) mma_commit(smem_u32(&bar));
+      __syncwarp();
+    };
+    auto wait_all = [&](uint64_t& bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(&bar), parity, abort_flag));
+    };
+    bool ok = wait_all(bars.q_full, 0);
+    for (int j = 0; ok && j < n_kt; ++j) {
+      const int s = j % NST;
+      const uint32_t ph = (uint32_t)(j / NST) & 1;
+      if (!(ok = wait_all(bars.k_full[s], ph))) break;
+      fence_after_sync();
+      qk(0, j);
+      commit(bars.s_full[0]);
+      if (n_qt == 2) {
+        if (j > 0) {
+          if (!(ok = wait_all(bars.p_full[1], (uint32_t)(j - 1) & 1))) break;
           fence_after_sync();
-          pv(1, n_kt - 1);
-          mma_commit(smem_u32(&bars.v_empty[(n_kt - 1) % NST]));
+          pv(1, j - 1);
+          commit(bars.v_empty[(j - 1) % NST]);
         }
+        qk(1, j);
+        commit(bars.s_full[1]);
       }
-      mma_commit(smem_u32(&bars.o_full));  // also on abort: tracks whatever was issued
+      commit(bars.k_empty[s]);
+      if (!(ok = wait_all(bars.v_full[s], ph))) break;
+      if (!(ok = wait_all(bars.p_full[0], (uint32_t)j & 1))) break;
+      fence_after_sync();
+      pv(0, j);
+      if (n_qt == 1) commit(bars.v_empty[s]);
     }
+    if (ok && n_qt == 2) {
+      if (wait_all(bars.p_full[1], (uint32_t)(n_kt - 1) & 1)) {
+        fence_after_sync();
+        pv(1, n_kt - 1);
+        commit(bars.v_empty[(n_kt - 1) % NST]);
+      }
+    }
+    commit(bars.o_full);  // also on abort: tracks whatever was issued
   }
   } else {
     regs_inc<kRegsHigh>();
@@ -305,48 +316,46 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
           }
         }
         tmem_ld_wait();
-        // row max (raw scores; the scale c > 0 is applied once), 8 independent chains
-        float mm[8];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) mm[a] = -INFINITY;
+        // row max (raw scores; the scale c > 0 is applied once): three-input max, 4 chains
+        float mm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (full) {
 #pragma unroll
-          for (int i = 0; i < BN; ++i) mm[i & 7] = fmaxf(mm[i & 7], __uint_as_float(sv[i]));
+          for (int i = 0; i < BN / 2; ++i)
+            mm[i & 3] = max3(mm[i & 3], __uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
         } else {
 #pragma unroll
           for (int i = 0; i < BN; ++i)
-            mm[i & 7] = ((vis[i >> 5] >> (i & 31)) & 1u) ? fmaxf(mm[i & 7], __uint_as_float(sv[i])) : mm[i & 7];
+            mm[i & 3] = ((vis[i >> 5] >> (i & 31)) & 1u) ? fmaxf(mm[i & 3], __uint_as_float(sv[i])) : mm[i & 3];
         }
-        const float mx = fmaxf(fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3])),
-                               fmaxf(fmaxf(mm[4], mm[5]), fmaxf(mm[6], mm[7])));
+        const float mx = fmaxf(max3(mm[0], mm[1], mm[2]), mm[3]);
         const float m_tile = (mx == -INFINITY) ? -INFINITY : mx * c;
         const bool grow = m_tile > m_ref + kRescaleLog2 || (m_ref == -INFINITY && m_tile != -INFINITY);
         const bool rescale = grow && m_ref != -INFINITY;
         const float alpha = rescale ? ex2(m_ref - m_tile) : 1.f;
         if (grow) m_ref = m_tile;
         const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-        // P = exp2(S*c - m) (3 of 4 on MUFU, 1 of 4 on the FMA pipe), 16-bit, into the first 64 columns of S
-        float rsum[4] = {0.f, 0.f, 0.f, 0.f};
+        // P = exp2(S*c - m) in packed pairs (f32x2 FMA / add), 16-bit, into the first 64 columns of S
+        const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
+        float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int e = cc * 32 + 2 * i;
-            const float x0 = fmaf(__uint_as_float(sv[e]), c, -m_use);
-            const float x1 = fmaf(__uint_as_float(sv[e + 1]), c, -m_use);
-            float p0 = ex2(x0);
-            float p1 = (i & 1) ? ex2_poly(x1) : ex2(x1);
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), c2, nm2);
+            float p0 = ex2(x.x);
+            float p1 = ex2(x.y);
             if (!full) {
               p0 = ((vis[cc] >> (2 * i)) & 1u) ? p0 : 0.f;
               p1 = ((vis[cc] >> (2 * i + 1)) & 1u) ? p1 : 0.f;
             }
-            rsum[i & 3] += p0 + p1;
+            acc[i & 1] = __fadd2_rn(acc[i & 1], make_float2(p0, p1));
             pk[i] = pack2<BF16>(p0, p1);
           }
           tmem_st16(S_t + cc * 16, pk);
         }
-        l = l * alpha + ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3]));
+        l = l * alpha + ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));
         // lazy correction of O (rows whose max grew by more than 2^8); PV_{j-1} is complete
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll

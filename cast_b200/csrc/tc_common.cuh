@@ -86,6 +86,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
+// One lane of a converged warp (the same lane every time: the lowest active one).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ---- register reallocation between warpgroups ------------------------------------
 // Executed by all 128 threads of a warpgroup. The block's register pool is
 // its launch allocation (threads x registers at launch): decreases by some
