@@ -269,18 +269,23 @@ def run_cast(args):
     attn_tflops = call_flops / (attn_ms * 1e-3) / 1e12     # per GPU, dominant kernel, per call
     attn_gbs = call_bytes / (attn_ms * 1e-3) / 1e9
     topk_gbs = w.topk_bytes() / (tree_ms * 1e-3) / 1e9
-    # binding roofline of the attention kernel: the slower of the HBM and tensor floors
+    # binding roofline of the attention kernel: the slower of the HBM and tensor floors. The
+    # kernel runs `layers` times back to back inside a long step (power-capped clocks), so the
+    # tensor peak is the sustained figure; the burst figure is reported beside it.
+    tf_peak = tf_sus
     t_hbm = call_bytes / (hbm * 1e9)
-    t_tensor = call_flops / (tf_burst * 1e12)
+    t_tensor = call_flops / (tf_peak * 1e12)
     bound = "tensor" if t_tensor >= t_hbm else "hbm"
     if bound == "tensor":
-        roof = {"bound": "tensor", "achieved": round(attn_tflops, 2), "peak": tf_burst, "unit": "TFLOP/s",
-                "frac": round(attn_tflops / tf_burst, 4)}
+        roof = {"bound": "tensor", "achieved": round(attn_tflops, 2), "peak": tf_peak, "unit": "TFLOP/s",
+                "frac": round(attn_tflops / tf_peak, 4)}
     else:
         roof = {"bound": "hbm", "achieved": round(attn_gbs, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(attn_gbs / hbm, 4)}
     roof["traffic"] = _profile_traffic("attn_config3")
-    roof["peak_source"] = f"{peak_kind} (MEASURED_PEAKS.json burst figure; kernel timed alone per launch)"
+    roof["peak_source"] = (f"{peak_kind}: MEASURED_PEAKS.json bf16_tflops_sustained (kernel timed inside a long "
+                           f"step); hbm_gbs for the HBM floor")
+    roof["frac_of_burst_peak"] = round(attn_tflops / tf_burst, 4)
     roof["hbm_floor_us"] = round(t_hbm * 1e6, 1)
     roof["tensor_floor_us"] = round(t_tensor * 1e6, 1)
 

@@ -292,41 +292,45 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
         ok = mbar_wait(smem_u32(&bars.s_full[q]), (uint32_t)j & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         fence_after_sync();
+        const int n0 = k_begin + j * BN;
+        const bool full = (n0 + BN <= m.S) && (n0 + BN <= k_end);
+        // visibility bits of the 128 keys (only tiles that reach the pack or the chunk end)
+        auto mask32 = [&](int nb) -> uint32_t {
+          uint32_t bits = 0;
+#pragma unroll 1
+          for (int i = 0; i < 32; ++i) {
+            const int n = nb + i;
+            bool ok_k = n < k_end;
+            if (ok_k && n >= m.S) {
+              const int jj = n - m.S;
+              ok_k = (anc[jj >> 6] >> (jj & 63)) & 1ull;
+            }
+            bits |= (ok_k ? 1u : 0u) << i;
+          }
+          return bits;
+        };
+        uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
+        if (!full) {
+          vis[0] = mask32(n0);
+          vis[1] = mask32(n0 + 32);
+          vis[2] = mask32(n0 + 64);
+          vis[3] = mask32(n0 + 96);
+        }
         // the whole 128-column row of S in one round trip
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) tmem_ld32(S_t + cc * 32, sv + cc * 32);
-        const int n0 = k_begin + j * BN;
-        const bool full = (n0 + BN <= m.S) && (n0 + BN <= k_end);
-        uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
-        if (!full) {
-#pragma unroll 1
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t bits = 0;
-#pragma unroll 1
-            for (int i = 0; i < 32; ++i) {
-              const int n = n0 + cc * 32 + i;
-              bool ok_k = n < k_end;
-              if (ok_k && n >= m.S) {
-                const int jj = n - m.S;
-                ok_k = (anc[jj >> 6] >> (jj & 63)) & 1ull;
-              }
-              bits |= (ok_k ? 1u : 0u) << i;
-            }
-            vis[cc] = bits;
-          }
-        }
         tmem_ld_wait();
-        // row max (raw scores; the scale c > 0 is applied once): three-input max, 4 chains
-        float mm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (full) {
-#pragma unroll
-          for (int i = 0; i < BN / 2; ++i)
-            mm[i & 3] = max3(mm[i & 3], __uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
-        } else {
+        if (!full) {
+          // invisible keys become -inf: the max ignores them and exp2 gives 0
 #pragma unroll
           for (int i = 0; i < BN; ++i)
-            mm[i & 3] = ((vis[i >> 5] >> (i & 31)) & 1u) ? fmaxf(mm[i & 3], __uint_as_float(sv[i])) : mm[i & 3];
+            sv[i] = ((vis[i >> 5] >> (i & 31)) & 1u) ? sv[i] : 0xff800000u;
         }
+        // row max (raw scores; the scale c > 0 is applied once): three-input max, 4 chains
+        float mm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < BN / 2; ++i)
+          mm[i & 3] = max3(mm[i & 3], __uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
         const float mx = fmaxf(max3(mm[0], mm[1], mm[2]), mm[3]);
         const float m_tile = (mx == -INFINITY) ? -INFINITY : mx * c;
         const bool grow = m_tile > m_ref + kRescaleLog2 || (m_ref == -INFINITY && m_tile != -INFINITY);
@@ -344,12 +348,8 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
           for (int i = 0; i < 16; ++i) {
             const int e = cc * 32 + 2 * i;
             const float2 x = __ffma2_rn(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), c2, nm2);
-            float p0 = ex2(x.x);
-            float p1 = ex2(x.y);
-            if (!full) {
-              p0 = ((vis[cc] >> (2 * i)) & 1u) ? p0 : 0.f;
-              p1 = ((vis[cc] >> (2 * i + 1)) & 1u) ? p1 : 0.f;
-            }
+            const float p0 = ex2(x.x);
+            const float p1 = ex2(x.y);
             acc[i & 1] = __fadd2_rn(acc[i & 1], make_float2(p0, p1));
             pk[i] = pack2<BF16>(p0, p1);
           }
