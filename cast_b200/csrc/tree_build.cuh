@@ -15,13 +15,13 @@ namespace cast {
 //  * sum_t = sum of exp(x - ref_t) against a reference ref_t that moves only
 //    when an element exceeds it by more than 2^8 nats worth of headroom (so
 //    the sum never overflows; fp64 keeps its relative precision at any scale),
-//  * its 4 best (x, index) candidates, sorted by x descending; a thread visits
+//  * its 8 best (x, index) candidates, sorted by x descending; a thread visits
 //    its elements in increasing index order, so an equal x never displaces an
 //    earlier one (the stable sort's lower-index-first rule).
 // The CTA merges the thread lists into its KC best by (x desc, index asc).
-// That set is exactly the row's KC best unless some thread's 4th candidate is
-// itself among them (the thread may have dropped a 5th): such rows take the
-// exact path below. With M the max and lse = log(sum exp(x - M)), the KC
+// That set is exactly the row's KC best unless some thread's 8th candidate is
+// itself among them (the thread may have dropped a 9th): such rows take the
+// exact path below. The row max M is the best candidate. With M the max and lse = log(sum exp(x - M)), the KC
 // candidates get lp = (x - M) - lse (the reference's operation order) and are
 // re-sorted by (lp desc, index asc); rounding in that subtraction can map
 // distinct x to one lp, so when the k-th and KC-th lp are equal an element
@@ -31,16 +31,18 @@ namespace cast {
 namespace topk {
 constexpr int NT = 256;
 constexpr int NW = NT / 32;
-constexpr int TL = 4;  // candidates per thread in the common path
+constexpr int TL = 8;  // candidates per thread in the common path
 }
 
 // exp(t) in float64 for t <= 709, written from the mathematics: Cody-Waite
 // reduction t = k ln2 + r with ln 2 split into a 33-bit head (k * head exact
-// for |k| < 2^20) and its tail, |r| <= ln2/2, then the degree-12 Taylor
-// polynomial of e^r by Horner's rule (truncation < 2e-16 relative) and an
-// exponent-field scale by 2^k. Results below 2^-1022 are returned as 0: such
-// terms are more than 700 nats below the running reference and cannot move a
-// sum that includes a term of size 1.
+// for |k| < 2^20) and its tail, |r| <= ln2/2, then the degree-10 Taylor
+// polynomial of e^r by Horner's rule (truncation < 2.3e-13 relative: the
+// log-sum it feeds is then within 2.3e-13 absolute, far inside the 1e-12
+// relative bound on log-probs) and an exponent-field scale by 2^k. Results
+// below 2^-1022 are returned as 0: such terms are more than 700 nats below the
+// running reference and cannot move a sum that includes a term of size 1.
+// The kernel is bound by the float64 pipe, so the degree is kept minimal.
 __device__ __forceinline__ double exp_fast(double t) {
   constexpr double kLog2e = 1.4426950408889634;
   constexpr double kLn2Hi = 0.6931471803691238;        // 0x1.62e42fee00000p-1
@@ -50,9 +52,7 @@ __device__ __forceinline__ double exp_fast(double t) {
   const int k = (int)(__double_as_longlong(kd) & 0xFFFFFFFFll);
   const double kf = kd - kShift;
   const double r = fma(-kf, kLn2Lo, fma(-kf, kLn2Hi, t));
-  double p = 2.08767569878681e-09;                    // 1/12!
-  p = fma(p, r, 2.505210838544172e-08);               // 1/11!
-  p = fma(p, r, 2.755731922398589e-07);               // 1/10!
+  double p = 2.755731922398589e-07;                   // 1/10!
   p = fma(p, r, 2.7557319223985893e-06);              // 1/9!
   p = fma(p, r, 2.48015873015873e-05);                // 1/8!
   p = fma(p, r, 0.0001984126984126984);               // 1/7!
@@ -67,9 +67,8 @@ __device__ __forceinline__ double exp_fast(double t) {
   return p * __longlong_as_double((long long)(k + 1023) << 52);
 }
 
-// Folds one element into a thread's (max, reference, sum of exp(x - reference)).
-__device__ __forceinline__ void lse_add(double& mx, double& ref, double& s, double v) {
-  mx = fmax(mx, v);
+// Folds one element into a thread's (reference, sum of exp(x - reference)).
+__device__ __forceinline__ void lse_add(double& ref, double& s, double v) {
   if (v == -INFINITY) return;
   double t = v - ref;
   if (!(t <= 256.0)) {
@@ -215,13 +214,14 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
 
   CandList<TL> cl;
   cl.init();
-  double mx = -INFINITY, ref = -INFINITY, s = 0.0;
+  double ref = -INFINITY, s = 0.0;
   scan_row<VEC2>(x, V, [&](double v, int j) {
-    lse_add(mx, ref, s, v);
+    lse_add(ref, s, v);
     if (cl.wants(v)) cl.insert(v, j);
   });
-  const double my4x = cl.x[TL - 1];
-  const int my4i = cl.idx[TL - 1];
+  double mx = cl.idx[0] >= 0 ? cl.x[0] : -INFINITY;   // this thread's max
+  const double my_last_x = cl.x[TL - 1];
+  const int my_last_i = cl.idx[TL - 1];
 
   // (max, reference, sum): warp, then CTA
 #pragma unroll
@@ -238,8 +238,9 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
   if (lane == 0) { s_m[warp] = mx; s_r[warp] = ref; s_s[warp] = s; }
   merge_lists<KC, TL>(cl, s_cx, s_ci, s_fx, s_fi);
 
-  // a thread whose 4th candidate made the CTA's KC best may have dropped a 5th
-  const bool saturated = my4i >= 0 && s_fi[KC - 1] >= 0 && !cand_before(s_fx[KC - 1], s_fi[KC - 1], my4x, my4i);
+  // a thread whose last candidate made the CTA's KC best may have dropped one more
+  const bool saturated =
+      my_last_i >= 0 && s_fi[KC - 1] >= 0 && !cand_before(s_fx[KC - 1], s_fi[KC - 1], my_last_x, my_last_i);
   const int any_saturated = __syncthreads_or(saturated ? 1 : 0);
 
   if (tid == 0) {
@@ -299,7 +300,10 @@ block_topk_exact_kernel(const double* __restrict__ logits, int64_t V, int64_t ro
   const double* x = logits + row * row_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   double mx = -INFINITY, ref = -INFINITY, s = 0.0;
-  scan_row<VEC2>(x, V, [&](double v, int) { lse_add(mx, ref, s, v); });
+  scan_row<VEC2>(x, V, [&](double v, int) {
+    mx = fmax(mx, v);
+    lse_add(ref, s, v);
+  });
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
     mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, off));
