@@ -9,7 +9,8 @@ package is the Python face of that library and has no CPU fallback.
 __version__ = "0.1.0"
 
 from .tree import TreeNode, Trees, block_topk, block_topk_device, build_tree, build_trees
-from .tree_attn import attention_plan, varlen_tree_attention, workspace_size
+from .tree_attn import attention_plan, varlen_tree_attention, varlen_tree_attention_store, workspace_size
 
 __all__ = ["TreeNode", "Trees", "block_topk", "block_topk_device", "build_tree", "build_trees",
-           "varlen_tree_attention", "workspace_size", "attention_plan", "__version__"]
+           "varlen_tree_attention", "varlen_tree_attention_store", "workspace_size", "attention_plan",
+           "__version__"]

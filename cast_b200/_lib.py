@@ -28,7 +28,7 @@ CAST_MAX_DEPTH = 64
 # every symbol include/cast_b200.h declares
 EXPORTS = ("cast_strerror", "cast_version", "cast_device_error", "cast_tree_attn_fwd",
            "cast_tree_attn_workspace_size", "cast_tree_attn_plan", "cast_block_topk", "cast_build_tree",
-           "cast_tree_attn_fwd_noalloc")
+           "cast_tree_attn_fwd_noalloc", "cast_tree_attn_store_fwd", "cast_tree_attn_store_workspace_size")
 CAST_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 
@@ -91,6 +91,13 @@ def lib():
                                              c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_vp,
                                              c_int, c_int, c_int, c_int, c_int, c_int,
                                              ctypes.c_float, c_int, c_int, c_vp]
+    L.cast_tree_attn_store_fwd.restype = c_int
+    L.cast_tree_attn_store_fwd.argtypes = [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_vp,
+                                           c_vp, c_vp, c_vp, c_vp, c_int, c_vp,
+                                           c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                           ctypes.c_float, c_int, c_int, c_vp, c_sz, c_vp]
+    L.cast_tree_attn_store_workspace_size.restype = c_sz
+    L.cast_tree_attn_store_workspace_size.argtypes = [c_int] * 8
     L.cast_tree_attn_plan.restype = c_int
     L.cast_tree_attn_plan.argtypes = [c_int] * 8 + [c_vp] * 6
     L.cast_tree_attn_workspace_size.restype = c_sz

@@ -39,7 +39,19 @@ struct AttnParams {
   int n_split, chunk, m_tiles, W;
   float* ws_o;   // [n_split, total_q, H_q, D]
   float* ws_ml;  // [n_split, total_q, H_q, 2]
+  // Store mode (tensor-core kernel only): the prefix of sequence b is rows
+  // [0, S_b) of a per-request store [store_batch, H_kv, store_rows, D], the
+  // pack K/V rows [cu_q[b], cu_q[b] + P_b) of [total_q, H_kv, D] tensors; the
+  // key tiles are ceil(S_b/128) prefix tiles then ceil(P_b/128) pack tiles.
+  int store_mode;
+  int store_rows, store_batch;
 };
+
+// Key tiles of one sequence: the whole range for the regular layout, the
+// prefix tiles plus the pack tiles for the store layout.
+__device__ __forceinline__ int seq_key_tiles(const AttnParams& p, int S, int P, int bn) {
+  return p.store_mode ? (S + bn - 1) / bn + (P + bn - 1) / bn : (S + P + bn - 1) / bn;
+}
 
 namespace simt {
 constexpr int BM = 64, BN = 64, NT = 256;
@@ -289,10 +301,18 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnParams p) {
     if (p.cu_q[mid] <= t) lo = mid; else hi = mid - 1;
   }
   const int b = lo;
-  const SeqMeta m = load_seq(p.cu_q, p.cu_kv, p.prefix_len, p.pack_len, b, p.total_q, p.total_kv,
-                             p.max_pack, p.max_kv);
+  SeqMeta m;
+  if (p.store_mode) {
+    m.q0 = p.cu_q[b]; m.kv0 = 0; m.S = p.prefix_len[b]; m.P = p.pack_len[b];
+    m.ok = m.q0 >= 0 && m.S >= 0 && m.P >= 0 && m.P <= p.max_pack && m.S <= p.store_rows &&
+           (long long)m.q0 + m.P <= p.total_q;
+  } else {
+    m = load_seq(p.cu_q, p.cu_kv, p.prefix_len, p.pack_len, b, p.total_q, p.total_kv, p.max_pack, p.max_kv);
+  }
   if (!m.ok || t < m.q0 || t >= m.q0 + m.P) return;
-  const int nsplit = min(p.n_split, (m.S + m.P + p.chunk - 1) / p.chunk);
+  const int tiles_per_chunk = p.chunk / 128;
+  const int nsplit = p.store_mode ? min(p.n_split, (seq_key_tiles(p, m.S, m.P, 128) + tiles_per_chunk - 1) / tiles_per_chunk)
+                                  : min(p.n_split, (m.S + m.P + p.chunk - 1) / p.chunk);
   float M = -INFINITY;
   for (int z = 0; z < nsplit; ++z)
     M = fmaxf(M, p.ws_ml[(((int64_t)z * p.total_q + t) * p.H_q + hq) * 2]);

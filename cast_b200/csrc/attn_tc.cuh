@@ -86,10 +86,14 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
-template <bool BF16>
+// STORE = false: K/V are [total_kv, H_kv, D] (tmK, tmV; tmKp/tmVp unused).
+// STORE = true: tmK/tmV map the per-request prefix stores [B, H_kv, S_max, D]
+// (4-D), tmKp/tmVp the pack K/V [total_q, H_kv, D].
+template <bool BF16, bool STORE>
 __global__ void __launch_bounds__(NT, 1)
 attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-               const __grid_constant__ CUtensorMap tmV) {
+               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKp,
+               const __grid_constant__ CUtensorMap tmVp) {
   using namespace tc;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -100,8 +104,14 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.y / p.H_kv, h = blockIdx.y % p.H_kv;
-  const SeqMeta m = load_seq(p.cu_q, p.cu_kv, p.prefix_len, p.pack_len, b, p.total_q, p.total_kv, p.max_pack,
-                             p.max_kv);
+  SeqMeta m;
+  if constexpr (STORE) {
+    m.q0 = p.cu_q[b]; m.kv0 = 0; m.S = p.prefix_len[b]; m.P = p.pack_len[b];
+    m.ok = m.q0 >= 0 && m.S >= 0 && m.P >= 0 && m.P <= p.max_pack && m.S <= p.store_rows && b < p.store_batch &&
+           (long long)m.q0 + m.P <= p.total_q;
+  } else {
+    m = load_seq(p.cu_q, p.cu_kv, p.prefix_len, p.pack_len, b, p.total_q, p.total_kv, p.max_pack, p.max_kv);
+  }
   if (!m.ok) {
     if (tid == 0 && blockIdx.x == 0 && blockIdx.z == 0) report(CAST_DEV_BAD_LAYOUT);
     return;
@@ -112,10 +122,37 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   if (r_base >= rows) return;
   const int n_qt = (rows - r_base > BM) ? 2 : 1;
   const int nkeys = m.S + m.P;
-  const int k_begin = blockIdx.z * p.chunk;
-  if (k_begin >= nkeys) return;
-  const int k_end = min(nkeys, k_begin + p.chunk);
-  const int n_kt = (k_end - k_begin + BN - 1) / BN;
+  // Key tiles of this CTA. Regular layout: keys [k_begin, k_end) of concat(prefix, pack),
+  // tile j at key k_begin + 128 j. Store layout: tiles [t_begin, t_begin + n_kt) of the
+  // list (prefix tiles, then pack tiles).
+  int k_begin, k_end, t_begin = 0, nt_pre = 0, n_kt;
+  if constexpr (STORE) {
+    nt_pre = (m.S + BN - 1) / BN;
+    const int nt_all = nt_pre + (m.P + BN - 1) / BN;
+    const int ct = p.chunk / BN;
+    t_begin = blockIdx.z * ct;
+    if (t_begin >= nt_all) return;
+    n_kt = min(nt_all, t_begin + ct) - t_begin;
+    k_begin = 0;
+    k_end = nkeys;
+  } else {
+    k_begin = blockIdx.z * p.chunk;
+    if (k_begin >= nkeys) return;
+    k_end = min(nkeys, k_begin + p.chunk);
+    n_kt = (k_end - k_begin + BN - 1) / BN;
+  }
+  // Tile j: its first key (position in concat(prefix, pack)) and the end of the visible range.
+  auto tile_keys = [&](int j, int& n0, int& klim) {
+    if constexpr (STORE) {
+      const int t = t_begin + j;
+      if (t < nt_pre) { n0 = t * BN; klim = m.S; }
+      else { n0 = m.S + (t - nt_pre) * BN; klim = nkeys; }
+    } else {
+      n0 = k_begin + j * BN;
+      klim = k_end;
+    }
+  };
+  const bool has_pack_tile = STORE ? (t_begin + n_kt > nt_pre) : (k_end > m.S);
   volatile int* abort_flag = &abort_sh;
 
   if (tid == 0) {
@@ -140,7 +177,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   if (warp == 0) tmem_alloc(smem_u32(&tmem_base_sh), 512);
   const int i_lo = r_base / G;
   const int i_hi = min(m.P - 1, (r_base + QT * BM - 1) / G);
-  if (k_end > m.S) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc);
+  if (has_pack_tile) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -167,13 +204,23 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       const int s = j % NST;
       const uint32_t use = (uint32_t)(j / NST);
       const int row = m.kv0 + k_begin + j * BN;
+      // one 128-key tile of K or V (two 64-column halves) into the ring slot
+      auto load_tile = [&](const CUtensorMap* m_reg, const CUtensorMap* m_pack, uint32_t dst, uint32_t bar) {
+        for (int hf = 0; hf < 2; ++hf) {
+          if constexpr (STORE) {
+            const int t = t_begin + j;
+            if (t < nt_pre) tma_load_4d(dst + hf * HALF_BYTES, m_reg, hf * 64, t * BN, h, b, bar);
+            else tma_load_3d(dst + hf * HALF_BYTES, m_pack, hf * 64, h, m.q0 + (t - nt_pre) * BN, bar);
+          } else {
+            tma_load_3d(dst + hf * HALF_BYTES, m_reg, hf * 64, h, row, bar);
+          }
+        }
+      };
       if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.k_empty[s]), (use - 1) & 1, abort_flag)))
         break;
       if (elect_one()) {
         mbar_expect_tx(smem_u32(&bars.k_full[s]), TILE_BYTES);
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_3d(smem_u32(smem + SMEM_K + s * TILE_BYTES + hf * HALF_BYTES), &tmK, hf * 64, h, row,
-                      smem_u32(&bars.k_full[s]));
+        load_tile(&tmK, &tmKp, smem_u32(smem + SMEM_K + s * TILE_BYTES), smem_u32(&bars.k_full[s]));
       }
       __syncwarp();
       if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.v_empty[s]), (use - 1) & 1, abort_flag))) {
@@ -182,9 +229,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       }
       if (elect_one()) {
         mbar_expect_tx(smem_u32(&bars.v_full[s]), TILE_BYTES);
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_3d(smem_u32(smem + SMEM_V + s * TILE_BYTES + hf * HALF_BYTES), &tmV, hf * 64, h, row,
-                      smem_u32(&bars.v_full[s]));
+        load_tile(&tmV, &tmVp, smem_u32(smem + SMEM_V + s * TILE_BYTES), smem_u32(&bars.v_full[s]));
       }
       __syncwarp();
       issued = j + 1;
@@ -254,6 +299,22 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       }
       commit(bars.k_empty[s]);
       if (!(ok = wait_all(bars.v_full[s], ph))) break;
+      if constexpr (STORE) {
+        // The last prefix tile also holds store rows past the prefix: their scores are
+        // masked, but 0 x (a non-finite stale value) would still poison P V, so those
+        // V rows are zeroed (whole 128-byte rows: the swizzle only permutes inside a row).
+        int n0, klim;
+        tile_keys(j, n0, klim);
+        if (n0 < m.S && n0 + BN > m.S) {
+          uint8_t* vt = smem + SMEM_V + s * TILE_BYTES;
+          for (int e = lane; e < (n0 + BN - m.S) * 16; e += 32) {
+            const int r = m.S - n0 + (e >> 4), c = e & 15;
+            *reinterpret_cast<uint4*>(vt + (c >> 3) * HALF_BYTES + r * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+      }
       if (!(ok = wait_all(bars.p_full[0], (uint32_t)j & 1))) break;
       fence_after_sync();
       pv(0, j);
@@ -292,15 +353,16 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
         ok = mbar_wait(smem_u32(&bars.s_full[q]), (uint32_t)j & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         fence_after_sync();
-        const int n0 = k_begin + j * BN;
-        const bool full = (n0 + BN <= m.S) && (n0 + BN <= k_end);
+        int n0, klim;
+        tile_keys(j, n0, klim);
+        const bool full = (n0 + BN <= m.S) && (n0 + BN <= klim);
         // visibility bits of the 128 keys (only tiles that reach the pack or the chunk end)
         auto mask32 = [&](int nb) -> uint32_t {
           uint32_t bits = 0;
 #pragma unroll 1
           for (int i = 0; i < 32; ++i) {
             const int n = nb + i;
-            bool ok_k = n < k_end;
+            bool ok_k = n < klim;
             if (ok_k && n >= m.S) {
               const int jj = n - m.S;
               ok_k = (anc[jj >> 6] >> (jj & 63)) & 1ull;

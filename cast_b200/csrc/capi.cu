@@ -120,6 +120,13 @@ TcPlan plan_tc(int B, int total_q, int H_q, int H_kv, int max_pack, int max_kv, 
   return pl;
 }
 
+// Store layout: key tiles per sequence are ceil(S/128) + ceil(P/128); plan on
+// that tile count (chunks stay whole numbers of tiles).
+TcPlan plan_tc_store(int B, int total_q, int H_q, int H_kv, int max_pack, int max_prefix, int sms) {
+  const int tiles = (max_prefix + tca::BN - 1) / tca::BN + (max_pack + tca::BN - 1) / tca::BN;
+  return plan_tc(B, total_q, H_q, H_kv, max_pack, tiles * tca::BN, sms);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static std::atomic<void*> fn{nullptr};
   void* f = fn.load(std::memory_order_acquire);
@@ -157,25 +164,37 @@ bool tc_eligible(int dtype, int D, int G, const int64_t* st, const void* q, cons
   return aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(out, 16);
 }
 
-int launch_tc(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
-  CUtensorMap mq, mk, mv;
-  const int G = p.G;
-  if (!make_map(&mq, p.q, dtype, p.total_q, p.H_q, p.sq_m, p.sq_h, G, tca::BM / G) ||
-      !make_map(&mk, p.k, dtype, p.total_kv, p.H_kv, p.sk_m, p.sk_h, 1, tca::BN) ||
-      !make_map(&mv, p.v, dtype, p.total_kv, p.H_kv, p.sv_m, p.sv_h, 1, tca::BN))
-    return CAST_ERR_LAUNCH;
+// 4-D map over a per-request store [batch, heads, rows, 128] (strides in elements,
+// dim stride 1): box = 64 dims x 128 rows of one head of one request, 128-byte swizzle.
+bool make_store_map(CUtensorMap* map, const void* base, int dtype, int batch, int heads, int64_t rows, int64_t s_b,
+                    int64_t s_h, int64_t s_r) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[4] = {128, (cuuint64_t)rows, (cuuint64_t)heads, (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)s_r * 2, (cuuint64_t)s_h * 2, (cuuint64_t)s_b * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)tca::BN, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == CAST_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool STORE>
+int launch_tc_maps(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st, const CUtensorMap& mq,
+                   const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mkp, const CUtensorMap& mvp) {
   p.n_split = pl.n_split;
   p.chunk = pl.chunk;
   p.m_tiles = pl.m_blocks;
   p.W = pl.W;
-  const size_t smem = tca::smem_bytes(G, pl.W);
+  const size_t smem = tca::smem_bytes(p.G, pl.W);
   dim3 grid(pl.m_blocks, p.B * p.H_kv, pl.n_split);
   if (dtype == CAST_BF16) {
-    cudaFuncSetAttribute(tca::attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    tca::attn_tc_kernel<true><<<grid, tca::NT, smem, st>>>(p, mq, mk, mv);
+    cudaFuncSetAttribute(tca::attn_tc_kernel<true, STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    tca::attn_tc_kernel<true, STORE><<<grid, tca::NT, smem, st>>>(p, mq, mk, mv, mkp, mvp);
   } else {
-    cudaFuncSetAttribute(tca::attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    tca::attn_tc_kernel<false><<<grid, tca::NT, smem, st>>>(p, mq, mk, mv);
+    cudaFuncSetAttribute(tca::attn_tc_kernel<false, STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    tca::attn_tc_kernel<false, STORE><<<grid, tca::NT, smem, st>>>(p, mq, mk, mv, mkp, mvp);
   }
   if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
   if (pl.n_split > 1) {
@@ -187,6 +206,17 @@ int launch_tc(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
   }
   return CAST_OK;
 }
+
+int launch_tc(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  const int G = p.G;
+  if (!make_map(&mq, p.q, dtype, p.total_q, p.H_q, p.sq_m, p.sq_h, G, tca::BM / G) ||
+      !make_map(&mk, p.k, dtype, p.total_kv, p.H_kv, p.sk_m, p.sk_h, 1, tca::BN) ||
+      !make_map(&mv, p.v, dtype, p.total_kv, p.H_kv, p.sv_m, p.sv_h, 1, tca::BN))
+    return CAST_ERR_LAUNCH;
+  return launch_tc_maps<false>(p, pl, dtype, st, mq, mk, mv, mk, mv);
+}
+
 
 }  // namespace
 }  // namespace cast
@@ -376,6 +406,80 @@ int cast_tree_attn_fwd_noalloc(const void* q, const void* k, const void* v, void
   return cast_tree_attn_fwd(q, k, v, out, dtype, strides, cu_q, cu_kv, prefix_len, pack_len, anc_words,
                             anc_words_per_row, parent, B, total_q, total_kv, H_q, H_kv, D, sm_scale, max_pack,
                             max_kv, scratch, need > 0 ? (size_t)CAST_NOALLOC_SCRATCH_BYTES : 0, stream);
+}
+
+size_t cast_tree_attn_store_workspace_size(int dtype, int B, int total_q, int H_q, int H_kv, int D, int max_pack,
+                                           int max_prefix) {
+  if (dtype == CAST_F32 || D != 128 || B <= 0 || total_q <= 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0) return 0;
+  return plan_tc_store(B, total_q, H_q, H_kv, max_pack, max_prefix, sm_count()).ws_bytes;
+}
+
+int cast_tree_attn_store_fwd(const void* q, const void* k_store, const void* v_store, const void* k_pack,
+                             const void* v_pack, void* out, int dtype, const int64_t* strides,
+                             const int32_t* cu_q, const int32_t* prefix_len, const int32_t* pack_len,
+                             const int64_t* anc_words, int anc_words_per_row, const int32_t* parent,
+                             int B, int total_q, int store_batch, int store_rows, int H_q, int H_kv, int D,
+                             float sm_scale, int max_pack, int max_prefix,
+                             void* workspace, size_t workspace_bytes, cast_stream_t stream) {
+  if (dtype != CAST_BF16 && dtype != CAST_F16) return CAST_ERR_DTYPE;
+  if (B < 0 || total_q < 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0 || max_pack < 0 || max_prefix < 0 ||
+      store_batch < 0 || store_rows < 0)
+    return CAST_ERR_SHAPE;
+  if (D != 128) return CAST_ERR_HEAD_DIM;
+  if (max_pack > CAST_MAX_PACK) return CAST_ERR_PACK;
+  if (B == 0 || total_q == 0 || max_pack == 0) return CAST_OK;
+  if (!q || !k_store || !v_store || !k_pack || !v_pack || !out || !strides || !cu_q || !prefix_len || !pack_len)
+    return CAST_ERR_NULL;
+  if ((anc_words == nullptr) == (parent == nullptr)) return CAST_ERR_MASK_MODE;
+  if (anc_words && anc_words_per_row < 1) return CAST_ERR_PACK;
+  if (store_batch < B || (max_prefix > 0 && store_rows < 1)) return CAST_ERR_SHAPE;
+  const int G = H_q / H_kv;
+  if (G < 1 || 128 % G != 0) return CAST_ERR_SHAPE;
+  // strides: q (3), k_store (4), v_store (4), k_pack (3), v_pack (3), out (3); dims innermost last
+  const int64_t* sq = strides;
+  const int64_t* sks = strides + 3;
+  const int64_t* svs = strides + 7;
+  const int64_t* skp = strides + 11;
+  const int64_t* svp = strides + 14;
+  const int64_t* so = strides + 17;
+  for (const int64_t* t3 : {sq, skp, svp, so})
+    if (t3[2] != 1 || t3[0] % 8 != 0 || t3[1] % 8 != 0) return CAST_ERR_ALIGN;
+  for (const int64_t* t4 : {sks, svs})
+    if (t4[3] != 1 || t4[0] % 8 != 0 || t4[1] % 8 != 0 || t4[2] % 8 != 0) return CAST_ERR_ALIGN;
+  if (!aligned(q, 16) || !aligned(k_store, 16) || !aligned(v_store, 16) || !aligned(k_pack, 16) ||
+      !aligned(v_pack, 16) || !aligned(out, 16))
+    return CAST_ERR_ALIGN;
+  const int sms = sm_count();
+  if (sms <= 0) return CAST_ERR_DEVICE;
+
+  AttnParams p{};
+  p.q = q; p.k = k_pack; p.v = v_pack; p.out = out;
+  p.sq_m = sq[0]; p.sq_h = sq[1];
+  p.sk_m = skp[0]; p.sk_h = skp[1];
+  p.sv_m = svp[0]; p.sv_h = svp[1];
+  p.so_m = so[0]; p.so_h = so[1];
+  p.cu_q = cu_q; p.cu_kv = nullptr; p.prefix_len = prefix_len; p.pack_len = pack_len;
+  p.anc_words = anc_words; p.anc_wpr = anc_words_per_row; p.parent = parent;
+  p.B = B; p.total_q = total_q; p.total_kv = 0; p.H_q = H_q; p.H_kv = H_kv; p.G = G; p.D = D;
+  const float scale = sm_scale > 0.f ? sm_scale : 1.0f / sqrtf((float)D);
+  p.scale_log2 = scale * kLog2e;
+  p.max_pack = max_pack; p.max_kv = max_prefix + max_pack;
+  p.store_mode = 1; p.store_rows = store_rows; p.store_batch = store_batch;
+
+  const TcPlan pl = plan_tc_store(B, total_q, H_q, H_kv, max_pack, max_prefix, sms);
+  if (pl.ws_bytes > 0) {
+    if (!workspace || workspace_bytes < pl.ws_bytes || !aligned(workspace, 16)) return CAST_ERR_WORKSPACE;
+    p.ws_o = static_cast<float*>(workspace);
+    p.ws_ml = p.ws_o + (size_t)pl.n_split * total_q * H_q * D;
+  }
+  CUtensorMap mq, mks, mvs, mkp, mvp;
+  if (!make_map(&mq, q, dtype, total_q, H_q, sq[0], sq[1], G, tca::BM / G) ||
+      !make_store_map(&mks, k_store, dtype, store_batch, H_kv, store_rows > 0 ? store_rows : 1, sks[0], sks[1], sks[2]) ||
+      !make_store_map(&mvs, v_store, dtype, store_batch, H_kv, store_rows > 0 ? store_rows : 1, svs[0], svs[1], svs[2]) ||
+      !make_map(&mkp, k_pack, dtype, total_q, H_kv, skp[0], skp[1], 1, tca::BN) ||
+      !make_map(&mvp, v_pack, dtype, total_q, H_kv, svp[0], svp[1], 1, tca::BN))
+    return CAST_ERR_LAUNCH;
+  return launch_tc_maps<true>(p, pl, dtype, static_cast<cudaStream_t>(stream), mq, mks, mvs, mkp, mvp);
 }
 
 int cast_block_topk(const double* logits, int64_t n_rows, int64_t V, int64_t row_stride, int k,

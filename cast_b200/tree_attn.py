@@ -111,3 +111,95 @@ def varlen_tree_attention(q, k, v, cu_q, cu_kv, prefix_len, pack_len, ancestor_m
         workspace.data_ptr() if ws_bytes > 0 else None, ws_bytes, stream)
     _lib.check(code, "cast_tree_attn_fwd")
     return out
+
+
+def _store_ready(t, rank):
+    st = t.stride()
+    return st[-1] == 1 and all(x % 8 == 0 for x in st[:-1]) and t.data_ptr() % 16 == 0
+
+
+def varlen_tree_attention_store(q, k_store, v_store, k_pack, v_pack, cu_q, prefix_len, pack_len,
+                                ancestor_mask=None, sm_scale=None, *, parent=None, max_pack=None, max_prefix=None,
+                                out=None, workspace=None):
+    """Tree attention with each request's prefix read in place from its KV store.
+
+    q: [total_q, H_q, D]; k_store / v_store: [B_store, H_kv, S_max, D], request
+    b's prefix = rows [0, prefix_len[b]) of store row b (the per-layer stores of
+    cast_trees/serving.py:190-205); k_pack / v_pack: [total_q, H_kv, D], this
+    pass's keys and values in pack order (e.g. ``key[0].transpose(0, 1)`` of the
+    hook's [1, H_kv, T, D] tensor, no copy). Output, masks and conventions as
+    varlen_tree_attention. This replaces the hook's per-layer assembly of a
+    ragged K/V copy (and its fp32 cast, cast_trees/serving.py:60-71) with the
+    kernel's own addressing: prefix tiles come from the store, pack tiles from
+    the pack tensors.
+
+    16-bit inputs with D = 128 and H_q / H_kv dividing 128 run the tensor-core
+    kernel directly; other inputs are assembled into the ragged layout on the
+    device (as the reference hook does) and run through varlen_tree_attention.
+    """
+    total_q, H_q, D = q.shape
+    Bs, H_kv, S_max, _ = k_store.shape
+    assert H_q % H_kv == 0
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if not q.is_cuda:
+        raise RuntimeError("cast_b200.varlen_tree_attention_store needs CUDA tensors (no CPU path)")
+    if (ancestor_mask is None) == (parent is None):
+        raise ValueError("pass exactly one of ancestor_mask and parent")
+    dev = q.device
+    B = int(pack_len.shape[0])
+    cu_q_t, prefix_t, pack_t = _i32(cu_q, dev), _i32(prefix_len, dev), _i32(pack_len, dev)
+    if max_pack is None:
+        max_pack = int(pack_t.max().item()) if B > 0 else 0
+    if max_prefix is None:
+        max_prefix = int(prefix_t.max().item()) if B > 0 else 0
+    G = H_q // H_kv
+    direct = (q.dtype in (torch.bfloat16, torch.float16) and D == 128 and 128 % G == 0 and
+              all(t.dtype == q.dtype for t in (k_store, v_store, k_pack, v_pack)) and
+              _store_ready(q, 3) and _store_ready(k_store, 4) and _store_ready(v_store, 4) and
+              _store_ready(k_pack, 3) and _store_ready(v_pack, 3))
+    if out is None:
+        out = torch.empty_like(q)
+    if not direct or not _store_ready(out, 3):
+        # assemble concat(prefix_b, pack_b) per request, then the regular kernel
+        S = prefix_t.cpu().tolist()
+        P = pack_t.cpu().tolist()
+        cq = cu_q_t.cpu().tolist()
+        cu_kv = [0]
+        for s_b, p_b in zip(S, P):
+            cu_kv.append(cu_kv[-1] + s_b + p_b)
+        k_rag = torch.empty((cu_kv[-1], H_kv, D), dtype=k_pack.dtype, device=dev)
+        v_rag = torch.empty_like(k_rag)
+        for b in range(B):
+            a = cu_kv[b]
+            k_rag[a:a + S[b]] = k_store[b, :, :S[b]].transpose(0, 1)
+            v_rag[a:a + S[b]] = v_store[b, :, :S[b]].transpose(0, 1)
+            k_rag[a + S[b]:a + S[b] + P[b]] = k_pack[cq[b]:cq[b] + P[b]]
+            v_rag[a + S[b]:a + S[b] + P[b]] = v_pack[cq[b]:cq[b] + P[b]]
+        res = varlen_tree_attention(q, k_rag, v_rag, cu_q_t, torch.tensor(cu_kv, dtype=torch.int32, device=dev),
+                                    prefix_t, pack_t, ancestor_mask, sm_scale, parent=parent, max_pack=max_pack,
+                                    max_kv=max(s + p for s, p in zip(S, P)) if B else 0)
+        out.copy_(res)
+        return out
+    anc_ptr, wpr, par_ptr = None, 0, None
+    if ancestor_mask is not None:
+        anc = torch.as_tensor(ancestor_mask, device=dev).to(torch.int64).reshape(total_q, -1).contiguous()
+        anc_ptr, wpr = anc.data_ptr(), int(anc.shape[1])
+    else:
+        par = _i32(parent, dev)
+        par_ptr = par.data_ptr()
+    L = _lib.lib()
+    ws_bytes = int(L.cast_tree_attn_store_workspace_size(_DTYPES[q.dtype], B, total_q, H_q, H_kv, D, max_pack,
+                                                         max_prefix))
+    if ws_bytes > 0 and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes):
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    strides = (ctypes.c_int64 * 20)(*q.stride(), *k_store.stride(), *v_store.stride(), *k_pack.stride(),
+                                    *v_pack.stride(), *out.stride())
+    code = L.cast_tree_attn_store_fwd(
+        q.data_ptr(), k_store.data_ptr(), v_store.data_ptr(), k_pack.data_ptr(), v_pack.data_ptr(), out.data_ptr(),
+        _DTYPES[q.dtype], ctypes.addressof(strides), cu_q_t.data_ptr(), prefix_t.data_ptr(), pack_t.data_ptr(),
+        anc_ptr, wpr, par_ptr, B, total_q, Bs, S_max, H_q, H_kv, D, float(sm_scale), int(max_pack),
+        int(max_prefix), workspace.data_ptr() if ws_bytes > 0 else None, ws_bytes,
+        torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(code, "cast_tree_attn_store_fwd")
+    return out

@@ -156,6 +156,41 @@ size_t cast_tree_attn_workspace_size(int dtype, int B, int total_q, int H_q, int
                                      int max_pack, int max_kv);
 
 /*
+ * Tree attention reading the prefix straight from a per-request KV store.
+ * Replaces the ragged K/V assembly of cast_trees/serving.py:60-71 (every layer
+ * copies each request's prefix from its store into one buffer, k_rag/v_rag,
+ * and casts q/k/v to fp32) together with the attention call it feeds.
+ *
+ * Sequence b's prefix keys are rows [0, prefix_len[b]) of request b of the
+ * stores k_store / v_store [store_batch, H_kv, store_rows, D] (the per-layer
+ * stores the serving loop keeps, cast_trees/serving.py:190-205); its pack keys
+ * are rows [cu_q[b], cu_q[b] + pack_len[b]) of k_pack / v_pack [total_q, H_kv, D]
+ * (the current pass's keys, already in pack order). Visibility, output and
+ * parent / ancestor conventions are those of cast_tree_attn_fwd.
+ * 16-bit inputs (CAST_BF16 / CAST_F16), D = 128, H_q / H_kv dividing 128.
+ * strides[20] = element strides of q (row, head, dim), k_store (batch, head,
+ * row, dim), v_store (same), k_pack (row, head, dim), v_pack, out; dim strides
+ * 1, every other stride a multiple of 8 elements, bases 16-byte aligned.
+ * max_prefix bounds prefix_len[b] (<= store_rows); workspace as returned by
+ * cast_tree_attn_store_workspace_size(). Store rows past prefix_len[b] are
+ * never part of the result, whatever they hold (non-finite values included).
+ * Returns CAST_ERR_DTYPE / CAST_ERR_HEAD_DIM / CAST_ERR_SHAPE / CAST_ERR_ALIGN
+ * for inputs outside that form (the Python wrapper then assembles the ragged
+ * layout and calls cast_tree_attn_fwd).
+ */
+int cast_tree_attn_store_fwd(const void* q, const void* k_store, const void* v_store, const void* k_pack,
+                             const void* v_pack, void* out, int dtype, const int64_t* strides,
+                             const int32_t* cu_q, const int32_t* prefix_len, const int32_t* pack_len,
+                             const int64_t* anc_words, int anc_words_per_row, const int32_t* parent,
+                             int B, int total_q, int store_batch, int store_rows, int H_q, int H_kv, int D,
+                             float sm_scale, int max_pack, int max_prefix,
+                             void* workspace, size_t workspace_bytes, cast_stream_t stream);
+
+/* Bytes of workspace cast_tree_attn_store_fwd needs for these sizes (0 is possible). */
+size_t cast_tree_attn_store_workspace_size(int dtype, int B, int total_q, int H_q, int H_kv, int D, int max_pack,
+                                           int max_prefix);
+
+/*
  * How cast_tree_attn_fwd would run for these arguments (pure host arithmetic):
  * plan[0] = 1 for the tcgen05 tensor-core kernel, 0 for the CUDA-core kernel;
  * plan[1] = number of key-range splits; plan[2] = kernel launches per call
