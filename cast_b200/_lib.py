@@ -24,11 +24,13 @@ CAST_F32, CAST_BF16, CAST_F16 = 0, 1, 2
 CAST_MAX_PACK = 1024
 CAST_MAX_TOPK = 24
 CAST_MAX_DEPTH = 64
+CAST_DEV_BAD_LAYOUT, CAST_DEV_BAD_PARENT, CAST_DEV_TIMEOUT, CAST_DEV_TREE_OVERFLOW = 1, 2, 4, 5
 
 # every symbol include/cast_b200.h declares
 EXPORTS = ("cast_strerror", "cast_version", "cast_device_error", "cast_tree_attn_fwd",
            "cast_tree_attn_workspace_size", "cast_tree_attn_plan", "cast_block_topk", "cast_build_tree",
-           "cast_tree_attn_fwd_noalloc", "cast_tree_attn_store_fwd", "cast_tree_attn_store_workspace_size")
+           "cast_tree_attn_fwd_noalloc", "cast_tree_attn_store_fwd", "cast_tree_attn_store_workspace_size",
+           "cast_tree_walk_greedy", "cast_select_global_topk", "cast_append_store", "cast_gather_cache")
 CAST_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 
@@ -108,6 +110,20 @@ def lib():
     L.cast_build_tree.argtypes = [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_int,
                                   c_vp, c_vp, c_vp, c_vp, c_vp,
                                   c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]
+    L.cast_tree_walk_greedy.restype = c_int
+    L.cast_tree_walk_greedy.argtypes = [c_vp, c_int, c_i64, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int,
+                                        c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]
+    L.cast_select_global_topk.restype = c_int
+    L.cast_select_global_topk.argtypes = [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_i64,
+                                          c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                          c_vp, c_vp, c_vp, c_i64, c_vp]
+    L.cast_append_store.restype = c_int
+    L.cast_append_store.argtypes = [c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_vp,
+                                    c_int, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_vp,
+                                    c_int, c_vp]
+    L.cast_gather_cache.restype = c_int
+    L.cast_gather_cache.argtypes = [c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_vp, c_vp, c_int,
+                                    c_vp, c_int, c_vp]
     _LIB = L
     return L
 

@@ -4,12 +4,19 @@
     python -m cast_b200.bench_case --what attn_store --config 3 --batch 32 --iters 3
     python -m cast_b200.bench_case --what topk --config 3 --batch 32 --iters 3
     python -m cast_b200.bench_case --what tree --config 3 --batch 32 --iters 3
+    python -m cast_b200.bench_case --what walk --config 3 --batch 64 --iters 20
+    python -m cast_b200.bench_case --what select --config 5 --batch 512 --iters 20
+    python -m cast_b200.bench_case --what append --config 3 --batch 64 --iters 20
 
 Builds the first `batch` sequences of the configuration (trees from the GPU
 tree builder), launches the chosen kernel `iters` times on one GPU and prints
 the mean CUDA-event time per launch. `attn_store` runs the same attention with
 the prefixes read in place from per-request stores [B, H_kv, S_max, D] and the
-pack K/V as strided [T, H_kv, D] views of [H_kv, T, D] tensors. Meant to be wrapped by ncu with a kernel
+pack K/V as strided [T, H_kv, D] views of [H_kv, T, D] tensors. `walk` runs
+the greedy walk over synthetic bf16 target logits [total_q, V] that follow each
+tree for a few levels; `select` splits a shared budget of 8 nodes per request
+over trees built at width 48; `append` appends each walk's accepted rows to
+32 layers of per-request stores in place. Meant to be wrapped by ncu with a kernel
 filter (`-k regex:attn_tc|block_topk|build_tree`).
 """
 import argparse
@@ -23,7 +30,7 @@ from cast_b200 import _lib, workloads
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--what", choices=["attn", "attn_store", "topk", "tree"], default="attn")
+    ap.add_argument("--what", choices=["attn", "attn_store", "topk", "tree", "walk", "select", "append"], default="attn")
     ap.add_argument("--config", type=int, default=3)
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--iters", type=int, default=3)
@@ -59,6 +66,36 @@ def main():
         args_store = (q, k_store, v_store, k_pack.transpose(0, 1), v_pack.transpose(0, 1), t(lay["cu_q"]),
                       t(lay["prefix_len"]), t(lay["pack_len"]), None)
 
+    if args.what in ("walk", "append"):
+        gen = torch.Generator(device=dev).manual_seed(7)
+        tl = torch.empty((lay["total_q"], w.V), dtype=torch.bfloat16, device=dev)
+        tl.normal_(generator=gen)
+        pp, ptok = trees.pack_parent, torch.zeros_like(trees.pack_parent)
+        # tokens: node tokens (root 0); plant the first child's token as each row's argmax
+        ptok = torch.where(pp >= 0, torch.randint(0, w.V, ptok.shape, device=dev, dtype=torch.int32), ptok)
+        rows = torch.arange(lay["total_q"], device=dev)
+        big = torch.iinfo(torch.int64).max
+        first_child = torch.full((lay["total_q"],), big, dtype=torch.int64, device=dev)
+        q0 = torch.repeat_interleave(t(lay["cu_q"][:-1]).long(), t(lay["pack_len"]).long())
+        par_abs = torch.where(pp >= 0, q0 + pp.long(), torch.full_like(q0, -1))
+        child_rows = rows[par_abs >= 0]
+        first_child.scatter_reduce_(0, par_abs[child_rows], child_rows, reduce="amin")
+        # a row follows its first child with probability 3/4 (mean accepted length near 4)
+        has = (first_child < big) & (torch.rand(first_child.shape, generator=gen, device=dev) < 0.75)
+        tl[rows[has], ptok[first_child[has]].long()] = 50.0
+        path_cap = lay["max_pack"] - 1
+        walk_out = cast_b200.walk_trees_greedy(tl, cu_q, pp, ptok, path_cap)
+    if args.what == "append":
+        n_layers, s_cap = 32, (max(w.S) + 320 + 255) // 256 * 256
+        sl_t = t(lay["prefix_len"])
+        mk = lambda: torch.zeros((w.B, w.H_kv, s_cap, w.D), dtype=torch.bfloat16, device=dev)
+        bk = [mk() for _ in range(n_layers)]
+        bv = [mk() for _ in range(n_layers)]
+        pk = [torch.randn((w.H_kv, lay["total_q"], w.D), device=dev).to(torch.bfloat16) for _ in range(n_layers)]
+        pv = [torch.randn((w.H_kv, lay["total_q"], w.D), device=dev).to(torch.bfloat16) for _ in range(n_layers)]
+    if args.what == "select":
+        sel_src = cast_b200.build_trees(idx, lp, 48, 8, max_budget=48)
+
     def once():
         if args.what == "attn":
             cast_b200.varlen_tree_attention(*args_attn, parent=trees.pack_parent, max_pack=lay["max_pack"],
@@ -68,6 +105,12 @@ def main():
                                                   max_prefix=max(w.S), out=out)
         elif args.what == "topk":
             cast_b200.block_topk_device(logits, 8, idx, lp)
+        elif args.what == "walk":
+            cast_b200.walk_trees_greedy(tl, cu_q, pp, ptok, path_cap, out=walk_out)
+        elif args.what == "select":
+            cast_b200.select_global_topk_device(sel_src, 8 * w.B, pack_capacity=w.B * 9)
+        elif args.what == "append":
+            cast_b200.append_store_inplace(bk, bv, sl_t, cu_q[:-1], walk_out.accepted, walk_out.keep, pk, pv)
         else:
             cast_b200.build_trees(idx, lp, budget, 8, max_budget=max(w.N), cu_q=cu_q, total_q=lay["total_q"])
 
@@ -81,8 +124,13 @@ def main():
     torch.cuda.synchronize()
     if _lib.device_error() != 0:
         raise RuntimeError("device error")
-    print(json.dumps({"what": args.what, "config": args.config, "batch": w.B,
-                      "us_per_launch": round(ev[0].elapsed_time(ev[1]) * 1e3 / args.iters, 1)}))
+    rec = {"what": args.what, "config": args.config, "batch": w.B,
+           "us_per_launch": round(ev[0].elapsed_time(ev[1]) * 1e3 / args.iters, 1)}
+    if args.what in ("walk", "append"):
+        acc = walk_out.accepted.cpu()
+        rec["mean_accepted"] = round(float(acc.float().mean()), 2)
+        rec["rows_read"] = int(acc.sum())    # logits rows the walk read: one per accepted token
+    print(json.dumps(rec))
 
 
 if __name__ == "__main__":

@@ -4,6 +4,7 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 #include <stdio.h>
+#include <algorithm>
 #include <atomic>
 #include <type_traits>
 
@@ -11,6 +12,7 @@
 #include "attn_simt.cuh"
 #include "attn_tc.cuh"
 #include "tree_build.cuh"
+#include "verify_ops.cuh"
 
 namespace cast {
 namespace {
@@ -269,7 +271,7 @@ const char* cast_strerror(int status) {
     case CAST_DEV_BAD_LAYOUT: return "device: cu_q/cu_kv/prefix_len/pack_len out of range or above max_pack/max_kv";
     case CAST_DEV_BAD_PARENT: return "device: parent array is not a forest in pack order (need -1 <= parent[i] < i, parent[0] = -1)";
     case CAST_DEV_TIMEOUT: return "device: a bounded wait gave up";
-    case CAST_DEV_TREE_OVERFLOW: return "device: budget above max_budget";
+    case CAST_DEV_TREE_OVERFLOW: return "device: budget above max_budget, or an accepted path longer than path_cap";
     default: return "unknown status";
   }
 }
@@ -527,6 +529,184 @@ int cast_build_tree(const int64_t* top_idx, const double* top_lp, int B, int L, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   build_tree_kernel<<<B, 32, smem, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
+}
+
+int cast_tree_walk_greedy(const void* logits, int dtype, int64_t row_stride, int V, const int32_t* cu_q,
+                          const int32_t* pack_parent, const int32_t* pack_token, int B, int total_q, int path_cap,
+                          int32_t* path, int32_t* accepted, int64_t* bonus, int32_t* keep, int64_t* tokens,
+                          cast_stream_t stream) {
+  if (dtype != CAST_F32 && dtype != CAST_BF16 && dtype != CAST_F16) return CAST_ERR_DTYPE;
+  if (B < 0 || total_q < 0 || V < 1 || row_stride < V || path_cap < 1) return CAST_ERR_SHAPE;
+  if (B == 0) return CAST_OK;
+  if (!logits || !cu_q || !pack_parent || !pack_token || !path || !accepted || !bonus) return CAST_ERR_NULL;
+  const int es = dtype == CAST_F32 ? 4 : 2;
+  const bool vec = aligned(logits, 16) && (row_stride * es) % 16 == 0;
+  const int sms = sm_count();
+  if (sms <= 0) return CAST_ERR_DEVICE;
+  int cs = 1;
+  while (cs < 8 && (int64_t)B * cs < sms) cs *= 2;
+  walk::WalkArgs a{logits, row_stride, V, cu_q, pack_parent, pack_token, B, total_q, path_cap,
+                   path, accepted, bonus, keep, tokens};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(B * cs));
+  cfg.blockDim = dim3(walk::NT);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaSuccess;
+#define CAST_WALK_LAUNCH(T)                                                          \
+  switch (cs) {                                                                      \
+    case 1: e = cudaLaunchKernelEx(&cfg, walk::tree_walk_kernel<T, 1>, a, vec); break; \
+    case 2: e = cudaLaunchKernelEx(&cfg, walk::tree_walk_kernel<T, 2>, a, vec); break; \
+    case 4: e = cudaLaunchKernelEx(&cfg, walk::tree_walk_kernel<T, 4>, a, vec); break; \
+    default: e = cudaLaunchKernelEx(&cfg, walk::tree_walk_kernel<T, 8>, a, vec); break; \
+  }
+  if (dtype == CAST_F32) { CAST_WALK_LAUNCH(float) }
+  else if (dtype == CAST_BF16) { CAST_WALK_LAUNCH(__nv_bfloat16) }
+  else { CAST_WALK_LAUNCH(__half) }
+#undef CAST_WALK_LAUNCH
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
+}
+
+int cast_select_global_topk(const int32_t* token, const int32_t* depth, const int32_t* parent, const double* score,
+                            const int32_t* count, int B, int max_nodes, int64_t total,
+                            int32_t* out_token, int32_t* out_depth, int32_t* out_parent, double* out_score,
+                            int32_t* out_count, int32_t* cu_q, const int32_t* root_token, const int32_t* seq_len,
+                            int32_t* pack_parent, int32_t* pack_token, int32_t* pack_pos, int64_t pack_capacity,
+                            cast_stream_t stream) {
+  if (B < 0 || max_nodes < 1 || max_nodes > sel::MAX_NODES || B > CAST_MAX_SELECT_TREES) return CAST_ERR_SHAPE;
+  if (B == 0) return CAST_OK;
+  if (!token || !depth || !parent || !score || !count || !out_token || !out_depth || !out_parent || !out_score ||
+      !out_count)
+    return CAST_ERR_NULL;
+  if ((pack_parent || pack_token || pack_pos) && !cu_q) return CAST_ERR_NULL;
+  if ((pack_token && !root_token) || (pack_pos && !seq_len)) return CAST_ERR_NULL;
+  if (cu_q && pack_capacity < 0) return CAST_ERR_SHAPE;
+  if ((const void*)out_token == token || (const void*)out_depth == depth || (const void*)out_parent == parent ||
+      (const void*)out_score == score)
+    return CAST_ERR_ALIGN;
+  sel::SelArgs a{token, depth, parent, score, count, B, max_nodes, total, out_token, out_depth, out_parent,
+                 out_score, out_count, cu_q, root_token, seq_len, pack_parent, pack_token, pack_pos, pack_capacity};
+  const size_t smem = (size_t)(2 * B + 1) * sizeof(int);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(sel::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return CAST_ERR_LAUNCH;
+  sel::select_kernel<<<1, sel::NT, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  return cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
+}
+
+}  // extern "C"
+
+namespace cast {
+namespace {
+// One row-gather launch per block of up to kvg::MAXL layers.
+int kv_gather(int n_layers, const void* const* src_kv, void* const* dst_kv, const void* const* pack_kv,
+              int64_t pack_offset_bytes, kvg::KvArgs a, int64_t grid_rows, cudaStream_t st) {
+  const bool v16 = a.row_bytes % 16 == 0 && a.src_sb % 16 == 0 && a.src_sh % 16 == 0 && a.src_sr % 16 == 0 &&
+                   a.dst_sb % 16 == 0 && a.dst_sh % 16 == 0 && a.dst_sr % 16 == 0 && a.pk_sb % 16 == 0 &&
+                   a.pk_sh % 16 == 0 && a.pk_st % 16 == 0 && pack_offset_bytes % 16 == 0;
+  const bool v4 = a.row_bytes % 4 == 0 && a.src_sb % 4 == 0 && a.src_sh % 4 == 0 && a.src_sr % 4 == 0 &&
+                  a.dst_sb % 4 == 0 && a.dst_sh % 4 == 0 && a.dst_sr % 4 == 0 && a.pk_sb % 4 == 0 &&
+                  a.pk_sh % 4 == 0 && a.pk_st % 4 == 0 && pack_offset_bytes % 4 == 0;
+  bool p16 = v16, p4 = v4;
+  for (int i = 0; i < 2 * n_layers; ++i) {
+    for (const void* p : {(const void*)src_kv[i], (const void*)dst_kv[i], (const void*)pack_kv[i]}) {
+      p16 = p16 && aligned(p, 16);
+      p4 = p4 && aligned(p, 4);
+    }
+  }
+  const unsigned gx = (unsigned)((grid_rows + kvg::ROWS_PER_CTA - 1) / kvg::ROWS_PER_CTA);
+  if (gx == 0) return CAST_OK;
+  for (int l0 = 0; l0 < n_layers; l0 += kvg::MAXL) {
+    const int nl = std::min(kvg::MAXL, n_layers - l0);
+    kvg::Layers ly{};
+    for (int l = 0; l < nl; ++l)
+      for (int kv = 0; kv < 2; ++kv) {
+        ly.src[l][kv] = src_kv[2 * (l0 + l) + kv];
+        ly.dst[l][kv] = dst_kv[2 * (l0 + l) + kv];
+        ly.pack[l][kv] = static_cast<const char*>(pack_kv[2 * (l0 + l) + kv]) + pack_offset_bytes;
+      }
+    a.L = nl;
+    dim3 grid(gx, (unsigned)(a.B_dst * a.H), (unsigned)nl);
+    if (p16) kvg::kv_gather_kernel<uint4><<<grid, kvg::NT, 0, st>>>(a, ly);
+    else if (p4) kvg::kv_gather_kernel<uint32_t><<<grid, kvg::NT, 0, st>>>(a, ly);
+    else kvg::kv_gather_kernel<uint16_t><<<grid, kvg::NT, 0, st>>>(a, ly);
+    if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  }
+  return CAST_OK;
+}
+}  // namespace
+}  // namespace cast
+
+extern "C" {
+
+int cast_append_store(int n_layers, const void* const* src_kv, void* const* dst_kv, const void* const* pack_kv,
+                      int elem_bytes, int H, int D, int B_src, int64_t src_cap, const int64_t* src_strides,
+                      int B_dst, int64_t dst_cap, const int64_t* dst_strides, int64_t pack_rows,
+                      const int64_t* pack_strides, const int32_t* rows, const int32_t* store_len,
+                      const int32_t* accepted, const int32_t* keep, int keep_stride, const int32_t* cu_q,
+                      int append_only, cast_stream_t stream) {
+  if (elem_bytes != 2 && elem_bytes != 4) return CAST_ERR_DTYPE;
+  if (n_layers < 0 || H < 1 || D < 1 || B_src < 0 || B_dst < 0 || src_cap < 0 || dst_cap < 0 || pack_rows < 0 ||
+      keep_stride < 0 || (int64_t)B_dst * H > 65535)
+    return CAST_ERR_SHAPE;
+  if (n_layers == 0 || B_dst == 0) return CAST_OK;
+  if (!src_kv || !dst_kv || !pack_kv || !src_strides || !dst_strides || !pack_strides || !store_len || !accepted ||
+      !keep)
+    return CAST_ERR_NULL;
+  for (int i = 0; i < 2 * n_layers; ++i)
+    if (!src_kv[i] || !dst_kv[i] || !pack_kv[i]) return CAST_ERR_NULL;
+  if (append_only) {
+    if (rows || B_dst != B_src || dst_cap != src_cap) return CAST_ERR_SHAPE;
+    for (int i = 0; i < 2 * n_layers; ++i)
+      if (src_kv[i] != dst_kv[i]) return CAST_ERR_SHAPE;
+    for (int i = 0; i < 3; ++i)
+      if (src_strides[i] != dst_strides[i]) return CAST_ERR_SHAPE;
+  }
+  const int64_t e = elem_bytes;
+  kvg::KvArgs a{};
+  a.H = H; a.row_bytes = D * elem_bytes; a.append_only = append_only ? 1 : 0;
+  a.B_src = B_src; a.B_dst = B_dst; a.src_cap = src_cap; a.dst_cap = dst_cap; a.pack_rows = pack_rows;
+  a.src_sb = src_strides[0] * e; a.src_sh = src_strides[1] * e; a.src_sr = src_strides[2] * e;
+  a.dst_sb = dst_strides[0] * e; a.dst_sh = dst_strides[1] * e; a.dst_sr = dst_strides[2] * e;
+  a.pk_sb = pack_strides[0] * e; a.pk_sh = pack_strides[1] * e; a.pk_st = pack_strides[2] * e;
+  a.rows = rows; a.store_len = store_len; a.accepted = accepted; a.keep = keep; a.keep_stride = keep_stride;
+  a.cu_q = cu_q;
+  const int64_t grid_rows = append_only ? keep_stride : dst_cap;
+  return kv_gather(n_layers, src_kv, dst_kv, pack_kv, 0, a, grid_rows, static_cast<cudaStream_t>(stream));
+}
+
+int cast_gather_cache(int n_layers, const void* const* src_kv, void* const* dst_kv, int elem_bytes, int B, int H,
+                      int D, int64_t src_len, const int64_t* src_strides, const int64_t* dst_strides, int n_prefix,
+                      const int32_t* keep, int n_keep, cast_stream_t stream) {
+  if (elem_bytes != 2 && elem_bytes != 4) return CAST_ERR_DTYPE;
+  if (n_layers < 0 || B < 0 || H < 1 || D < 1 || src_len < 0 || n_prefix < 0 || n_keep < 0 ||
+      n_prefix > src_len || (int64_t)B * H > 65535)
+    return CAST_ERR_SHAPE;
+  if (n_layers == 0 || B == 0 || n_prefix + n_keep == 0) return CAST_OK;
+  if (!src_kv || !dst_kv || !src_strides || !dst_strides || (n_keep > 0 && !keep)) return CAST_ERR_NULL;
+  for (int i = 0; i < 2 * n_layers; ++i)
+    if (!src_kv[i] || !dst_kv[i]) return CAST_ERR_NULL;
+  const int64_t e = elem_bytes;
+  kvg::KvArgs a{};
+  a.H = H; a.row_bytes = D * elem_bytes; a.append_only = 0;
+  a.B_src = B; a.B_dst = B; a.src_cap = src_len; a.dst_cap = (int64_t)n_prefix + n_keep;
+  a.pack_rows = src_len - n_prefix;
+  a.src_sb = src_strides[0] * e; a.src_sh = src_strides[1] * e; a.src_sr = src_strides[2] * e;
+  a.dst_sb = dst_strides[0] * e; a.dst_sh = dst_strides[1] * e; a.dst_sr = dst_strides[2] * e;
+  a.pk_sb = a.src_sb; a.pk_sh = a.src_sh; a.pk_st = a.src_sr;
+  a.rows = nullptr; a.store_len = nullptr; a.accepted = nullptr; a.s_const = n_prefix; a.a_const = n_keep;
+  static const int32_t kNoKeep = 0;
+  a.keep = n_keep > 0 ? keep : &kNoKeep;   // never read when n_keep == 0
+  a.keep_stride = 0; a.cu_q = nullptr;
+  return kv_gather(n_layers, src_kv, dst_kv, src_kv, (int64_t)n_prefix * a.src_sr, a, a.dst_cap,
+                   static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -36,6 +36,7 @@ class Trees(NamedTuple):
     pack_parent: Optional[torch.Tensor] = None   # int32 [total_q], pack-local
     pack_token: Optional[torch.Tensor] = None    # int32 [total_q]
     pack_pos: Optional[torch.Tensor] = None      # int32 [total_q]
+    cu_q: Optional[torch.Tensor] = None          # int32 [B+1] (select_global_topk_device output)
 
 
 def _stream(dev):
@@ -152,3 +153,76 @@ def build_tree(top_idx, top_lp, budget, k=8):
     tok, dep, par = (x[0, :n].cpu().tolist() for x in (t.token, t.depth, t.parent))
     sc = t.score[0, :n].cpu().tolist()
     return [TreeNode(int(a), int(b), int(c), float(d)) for a, b, c, d in zip(tok, dep, par, sc)]
+
+
+def select_global_topk_device(trees: Trees, total, *, root_token=None, seq_len=None, pack_capacity=None):
+    """Shared-budget split of a device forest (cast_trees/tree.py:63-82), in one launch.
+
+    trees: a Trees from build_trees. The `total` best nodes of the pooled
+    forest by (-score, tree, node) are kept; each tree keeps its nodes in
+    order with renumbered parents. The result is a Trees of the same width
+    with the new counts and, always, the packed layout of the selected trees
+    (cu_q [B+1], pack_parent, and pack_token / pack_pos when root_token /
+    seq_len are given). pack_capacity (default B + min(total, B * width))
+    sizes the pack arrays without a device-to-host read.
+    """
+    token, depth, parent, score, count = trees.token, trees.depth, trees.parent, trees.score, trees.count
+    dev = token.device
+    B, mb = token.shape
+    total = int(total)
+    if pack_capacity is None:
+        tot = total if total >= 0 else B * mb
+        pack_capacity = B + max(0, min(tot, B * mb))
+    o = [torch.empty_like(token), torch.empty_like(depth), torch.empty_like(parent), torch.empty_like(score),
+         torch.empty_like(count)]
+    cu_q = torch.empty((B + 1,), dtype=torch.int32, device=dev)
+    pack_parent = torch.empty((max(1, pack_capacity),), dtype=torch.int32, device=dev)
+    pack_token = pack_pos = None
+    rt_ptr = sl_ptr = None
+    if root_token is not None:
+        root_token = torch.as_tensor(root_token, device=dev).to(torch.int32).contiguous()
+        rt_ptr = root_token.data_ptr()
+        pack_token = torch.empty_like(pack_parent)
+    if seq_len is not None:
+        seq_len = torch.as_tensor(seq_len, device=dev).to(torch.int32).contiguous()
+        sl_ptr = seq_len.data_ptr()
+        pack_pos = torch.empty_like(pack_parent)
+    ptr = lambda t: None if t is None else t.data_ptr()
+    code = _lib.lib().cast_select_global_topk(
+        token.data_ptr(), depth.data_ptr(), parent.data_ptr(), score.data_ptr(), count.data_ptr(), B, mb, total,
+        o[0].data_ptr(), o[1].data_ptr(), o[2].data_ptr(), o[3].data_ptr(), o[4].data_ptr(), cu_q.data_ptr(),
+        rt_ptr, sl_ptr, pack_parent.data_ptr(), ptr(pack_token), ptr(pack_pos), int(pack_capacity),
+        _stream(dev))
+    _lib.check(code, "cast_select_global_topk")
+    return Trees(o[0], o[1], o[2], o[3], o[4], pack_parent, pack_token, pack_pos, cu_q)
+
+
+def select_global_topk(trees, total):
+    """Split a shared budget across requests by global best-first score.
+
+    Same contract as cast_trees/tree.py:63-82: a list of TreeNode lists in,
+    a list of TreeNode lists out (the first `total` nodes of the pool sorted
+    by (-score, request, node) are kept, in node order, parents renumbered);
+    computed on the GPU.
+    """
+    dev = _cuda_device()
+    B = len(trees)
+    if B == 0:
+        return []
+    mb = max(1, max(len(t) for t in trees))
+    tok = np.zeros((B, mb), dtype=np.int32)
+    dep = np.zeros((B, mb), dtype=np.int32)
+    par = np.full((B, mb), -1, dtype=np.int32)
+    sc = np.zeros((B, mb), dtype=np.float64)
+    cnt = np.array([len(t) for t in trees], dtype=np.int32)
+    for b, nodes in enumerate(trees):
+        for j, nd in enumerate(nodes):
+            tok[b, j], dep[b, j], par[b, j], sc[b, j] = nd.token, nd.depth, nd.parent, nd.score
+    t = lambda a: torch.from_numpy(a).to(dev)
+    src = Trees(t(tok), t(dep), t(par), t(sc), t(cnt))
+    out = select_global_topk_device(src, total)
+    _lib.raise_device_error("cast_select_global_topk")
+    n = out.count.cpu().tolist()
+    tok, dep, par, sc = (x.cpu().tolist() for x in (out.token, out.depth, out.parent, out.score))
+    return [[TreeNode(int(tok[b][i]), int(dep[b][i]), int(par[b][i]), float(sc[b][i])) for i in range(n[b])]
+            for b in range(B)]

@@ -8,6 +8,11 @@
  *   - cast_trees/tree.py:20-26         block_topk
  *   - cast_trees/tree.py:29-49         build_tree
  *   - cast_trees/serving.py:213-222    packed tok/pos/ancestor layout of one verify pass
+ *   - cast_trees/serving.py:60-71      per-layer ragged K/V assembly (store-mode attention)
+ *   - cast_trees/decode.py:85-103      walk_tree at temperature 0 (greedy walk)
+ *   - cast_trees/tree.py:63-82         select_global_topk
+ *   - cast_trees/serving.py:264-289    BatchedServer._append_store
+ *   - cast_trees/verify.py:48-60       gather_cache
  *
  * Conventions shared by every entry point:
  *   - All array arguments are DEVICE pointers owned by the caller. The library
@@ -62,6 +67,8 @@ enum cast_status {
 #define CAST_MAX_PACK 1024    /* largest pack (1 + N) the attention kernels accept */
 #define CAST_MAX_TOPK 24      /* largest k of block_topk / build_tree */
 #define CAST_MAX_DEPTH 64     /* largest L of build_tree */
+#define CAST_MAX_SELECT_TREES 16384  /* largest forest of cast_select_global_topk */
+#define CAST_MAX_SELECT_NODES 1024   /* largest tree (row width) of cast_select_global_topk */
 
 /* Human-readable text for a status code (never NULL). */
 const char* cast_strerror(int status);
@@ -230,6 +237,79 @@ int cast_build_tree(const int64_t* top_idx, const double* top_lp, int B, int L, 
                     const int32_t* root_token, int32_t* pack_token,
                     const int32_t* seq_len, int32_t* pack_pos,
                     cast_stream_t stream);
+
+/*
+ * Greedy tree walk of a verify pass, cast_trees/decode.py:85-103 at
+ * temperature 0, for every sequence at once (the per-request loop of
+ * cast_trees/serving.py:326-336). From the root (pack row 0) the walk picks
+ * argmax(logits[row]) (torch.argmax order: NaN first, then the larger value,
+ * then the lower index); if a child of the current node carries that token
+ * (lowest pack index first) it moves there, else that token is the bonus.
+ * logits: [total_q, V] rows in pack order (dtype CAST_F32/BF16/F16, row stride
+ * in elements); cu_q int32 [B+1]; pack_parent int32 [total_q] (pack-local,
+ * -1 = root); pack_token int32 [total_q] (the token each packed row carries).
+ * Outputs: path int32 [B, path_cap] (accepted node indices = pack row - 1,
+ * -1 padded), accepted int32 [B] (= len(path) + 1), bonus int64 [B];
+ * optional keep int32 [B, path_cap + 1] (0, then path + 1: the reference's
+ * keep list) and tokens int64 [B, path_cap + 1] (the committed tokens: path
+ * tokens, then the bonus), -1 padded. Only the rows on each accepted path are
+ * read. A path longer than path_cap records CAST_DEV_TREE_OVERFLOW.
+ */
+int cast_tree_walk_greedy(const void* logits, int dtype, int64_t row_stride, int V, const int32_t* cu_q,
+                          const int32_t* pack_parent, const int32_t* pack_token, int B, int total_q, int path_cap,
+                          int32_t* path, int32_t* accepted, int64_t* bonus, int32_t* keep, int64_t* tokens,
+                          cast_stream_t stream);
+
+/*
+ * Shared-budget split of a forest, cast_trees/tree.py:63-82
+ * select_global_topk: the first `total` nodes of the pool sorted by
+ * (-score, tree, node) are kept (total < 0 acts like Python's pool[:total]),
+ * each tree keeps its nodes in their original order and parents are
+ * renumbered (-1 when the parent is not kept).
+ * Inputs [B, max_nodes] (row b holds count[b] nodes, as cast_build_tree writes
+ * them): token, depth, parent (tree-local), score. Outputs of the same shape
+ * and out_count [B]; they must not be the input arrays.
+ * Optional packed layout of the selected trees (cast_trees/serving.py:213-222):
+ * cu_q int32 [B+1] (written), pack_parent / pack_token (needs root_token) /
+ * pack_pos (needs seq_len), each with room for pack_capacity rows.
+ */
+int cast_select_global_topk(const int32_t* token, const int32_t* depth, const int32_t* parent, const double* score,
+                            const int32_t* count, int B, int max_nodes, int64_t total,
+                            int32_t* out_token, int32_t* out_depth, int32_t* out_parent, double* out_score,
+                            int32_t* out_count, int32_t* cu_q, const int32_t* root_token, const int32_t* seq_len,
+                            int32_t* pack_parent, int32_t* pack_token, int32_t* pack_pos, int64_t pack_capacity,
+                            cast_stream_t stream);
+
+/*
+ * Accepted-path append into the per-request KV stores, every layer in one
+ * call: cast_trees/serving.py:264-289 BatchedServer._append_store.
+ * src_kv / dst_kv / pack_kv are HOST arrays of 2 * n_layers device pointers
+ * (layer l's K at [2l], V at [2l + 1]). Stores are [B, H, cap, D] (strides
+ * batch, head, row in elements; dim stride 1); pack K/V are the verify pass's
+ * [H, total_q, D] per-layer tensors (pack_strides = batch (0), head, row).
+ * For destination row nb (source row b = rows[nb], or nb when rows is NULL),
+ * head h, layer l: rows [0, store_len[b]) copy the source store, rows
+ * store_len[b] + j (j < accepted[b]) take pack row cu_q[b] + keep[b * keep_stride + j],
+ * and rows up to dst_cap are zeroed. append_only = 1 writes only the appended
+ * rows of a store in place (dst_kv == src_kv, rows NULL, same shape).
+ */
+int cast_append_store(int n_layers, const void* const* src_kv, void* const* dst_kv, const void* const* pack_kv,
+                      int elem_bytes, int H, int D, int B_src, int64_t src_cap, const int64_t* src_strides,
+                      int B_dst, int64_t dst_cap, const int64_t* dst_strides, int64_t pack_rows,
+                      const int64_t* pack_strides, const int32_t* rows, const int32_t* store_len,
+                      const int32_t* accepted, const int32_t* keep, int keep_stride, const int32_t* cu_q,
+                      int append_only, cast_stream_t stream);
+
+/*
+ * cast_trees/verify.py:48-60 gather_cache for every layer in one call: the
+ * destination [B, H, n_prefix + n_keep, D] gets the first n_prefix rows of the
+ * source [B, H, src_len, D] and then its rows n_prefix + keep[j]. src_kv /
+ * dst_kv as in cast_append_store; keep is a device int32 array; the
+ * destination must not overlap the source.
+ */
+int cast_gather_cache(int n_layers, const void* const* src_kv, void* const* dst_kv, int elem_bytes, int B, int H,
+                      int D, int64_t src_len, const int64_t* src_strides, const int64_t* dst_strides, int n_prefix,
+                      const int32_t* keep, int n_keep, cast_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -136,3 +136,30 @@ def walk_tree_greedy(parent, token, logits):
             return path, pick
         path.append(hit)
         cur = hit
+
+
+def select_global_topk(trees, total):
+    """Shared-budget split of a forest, cast_trees/tree.py:63-82.
+
+    trees: list of Tree. The pool of (score, tree, node) is ordered by
+    (-score, tree, node) - Python's sort, so -0.0 and 0.0 tie - and the first
+    `total` entries (Python slice semantics, negative totals included) are
+    kept; each tree keeps its nodes in order and parents are renumbered, -1
+    where the parent was not kept.
+    """
+    pool = [(float(t.score[j]), b, j) for b, t in enumerate(trees) for j in range(len(t))]
+    pool.sort(key=lambda e: (-e[0], e[1], e[2]))
+    keep = [set() for _ in trees]
+    for _, b, j in pool[:total]:
+        keep[b].add(j)
+    out = []
+    for b, t in enumerate(trees):
+        kept = sorted(keep[b])
+        remap = {-1: -1}
+        for new, old in enumerate(kept):
+            remap[old] = new
+        idx = np.array(kept, dtype=np.int64)
+        out.append(Tree(t.token[idx].astype(np.int64), t.depth[idx].astype(np.int64),
+                        np.array([remap.get(int(t.parent[i]), -1) for i in kept], dtype=np.int64),
+                        t.score[idx].astype(np.float64)))
+    return out

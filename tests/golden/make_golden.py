@@ -20,6 +20,11 @@ Files written next to this script:
   attn_ragged.npz   a seeded ragged scenario built like tests/test_tree_attn.py,
                     scored by that file's reference(), at a reduced head count
   walk.npz          decode.walk_tree greedy paths on seeded logits
+  select.npz        tree.select_global_topk on seeded forests (several totals,
+                    and a forest whose scores tie across trees)
+  append.npz        serving.BatchedServer._append_store on small seeded stores:
+                    append in place, compaction (a request leaves), growth
+  gather.npz        verify.gather_cache on a small seeded two-layer cache
 """
 import argparse
 import importlib
@@ -209,17 +214,133 @@ def walk(tree, decode):
     np.savez_compressed(HERE / "walk.npz", **out)
 
 
+def _forest_arrays(trees, prefix, out):
+    mb = max(1, max(len(t) for t in trees))
+    B = len(trees)
+    tok = np.zeros((B, mb), np.int64)
+    dep = np.zeros((B, mb), np.int64)
+    par = np.full((B, mb), -1, np.int64)
+    sc = np.zeros((B, mb), np.float64)
+    for b, nodes in enumerate(trees):
+        for j, nd in enumerate(nodes):
+            tok[b, j], dep[b, j], par[b, j], sc[b, j] = nd.token, nd.depth, nd.parent, nd.score
+    out[prefix + "token"], out[prefix + "depth"], out[prefix + "parent"], out[prefix + "score"] = tok, dep, par, sc
+    out[prefix + "count"] = np.array([len(t) for t in trees], np.int64)
+
+
+SELECT_TOTALS = (0, 1, 17, 64, 200, 10000, -5)
+
+
+def select(tree):
+    out = {}
+    rng = np.random.default_rng(31)
+    # seeded forests of unequal trees (the reference test's shape: 8 trees, budget 48)
+    forests = {"rand": [tree.build_tree(*tree.block_topk(rng.normal(scale=3, size=(15, 40))), budget=48)
+                        for _ in range(8)],
+               "ties": [tree.build_tree(*tree.block_topk(np.round(rng.normal(scale=2, size=(6, 5)))), budget=12)
+                        for _ in range(5)]}
+    # identical trees: every score ties across trees, so (tree, node) order decides
+    same = tree.build_tree(*tree.block_topk(rng.normal(scale=3, size=(8, 20))), budget=20)
+    forests["same"] = [same, same, same]
+    for name, trees in forests.items():
+        _forest_arrays(trees, f"{name}_in_", out)
+        for total in SELECT_TOTALS:
+            _forest_arrays(tree.select_global_topk(trees, total), f"{name}_t{total}_", out)
+    out["totals"] = np.array(SELECT_TOTALS, np.int64)
+    np.savez_compressed(HERE / "select.npz", **out)
+
+
+def append(serving):
+    """_append_store with a stand-in `self` (only .device is read) and PACK_KV set per case."""
+    out = {}
+    rng = np.random.default_rng(41)
+    g = torch.Generator().manual_seed(41)
+    L, H, D = 2, 2, 16
+    cases = {"inplace": dict(B=3, cap=12, store_len=[3, 5, 0], rows=[0, 1, 2]),
+             "compact": dict(B=4, cap=12, store_len=[4, 2, 6, 1], rows=[0, 2, 3]),
+             "grow": dict(B=3, cap=8, store_len=[6, 2, 7], rows=[1, 2])}
+    for name, c in cases.items():
+        B, cap, sl, rows = c["B"], c["cap"], c["store_len"], c["rows"]
+        buf_k = [torch.zeros((B, H, cap, D)) for _ in range(L)]
+        buf_v = [torch.zeros((B, H, cap, D)) for _ in range(L)]
+        for li in range(L):
+            for b in range(B):
+                buf_k[li][b, :, :sl[b]] = torch.randn(H, sl[b], D, generator=g)
+                buf_v[li][b, :, :sl[b]] = torch.randn(H, sl[b], D, generator=g)
+        pack = [int(rng.integers(3, 7)) for _ in range(B)]
+        cu_q = [0]
+        for p in pack:
+            cu_q.append(cu_q[-1] + p)
+        keep, accepted = [], []
+        for b in range(B):
+            path = sorted(rng.choice(np.arange(1, pack[b]), size=int(rng.integers(0, pack[b])), replace=False))
+            keep.append([0] + [int(x) for x in path])
+            accepted.append(len(path) + 1)
+        pk = [torch.randn(H, cu_q[-1], D, generator=g) for _ in range(L)]
+        pv = [torch.randn(H, cu_q[-1], D, generator=g) for _ in range(L)]
+        serving.PACK_KV["k"], serving.PACK_KV["v"] = pk, pv
+        me = types.SimpleNamespace(device=torch.device("cpu"))
+        ins_k = [x.clone() for x in buf_k]
+        ins_v = [x.clone() for x in buf_v]
+        nk, nv, new_len = serving.BatchedServer._append_store(me, buf_k, buf_v, sl, cu_q, keep, accepted, rows)
+        out[f"{name}_in_k"] = torch.stack(ins_k).numpy()
+        out[f"{name}_in_v"] = torch.stack(ins_v).numpy()
+        out[f"{name}_pack_k"] = torch.stack(pk).numpy()
+        out[f"{name}_pack_v"] = torch.stack(pv).numpy()
+        out[f"{name}_store_len"] = np.array(sl, np.int64)
+        out[f"{name}_cu_q"] = np.array(cu_q, np.int64)
+        out[f"{name}_rows"] = np.array(rows, np.int64)
+        out[f"{name}_accepted"] = np.array(accepted, np.int64)
+        kk = np.full((B, max(len(k) for k in keep)), -1, np.int64)
+        for b in range(B):
+            kk[b, :len(keep[b])] = keep[b]
+        out[f"{name}_keep"] = kk
+        out[f"{name}_out_k"] = torch.stack(nk).numpy()
+        out[f"{name}_out_v"] = torch.stack(nv).numpy()
+        out[f"{name}_new_len"] = np.array(new_len, np.int64)
+    np.savez_compressed(HERE / "append.npz", **out)
+
+
+def gather(verify):
+    g = torch.Generator().manual_seed(51)
+    L, B, H, S, D = 2, 1, 2, 20, 16
+    cache = types.SimpleNamespace(key_cache=[torch.randn(B, H, S, D, generator=g) for _ in range(L)],
+                                  value_cache=[torch.randn(B, H, S, D, generator=g) for _ in range(L)])
+    in_k = torch.stack(cache.key_cache).numpy().copy()
+    in_v = torch.stack(cache.value_cache).numpy().copy()
+    n_prefix, keep = 12, [0, 2, 3, 6]
+    verify.gather_cache(cache, n_prefix, keep)
+    np.savez_compressed(HERE / "gather.npz", in_k=in_k, in_v=in_v, n_prefix=np.int64(n_prefix),
+                        keep=np.array(keep, np.int64), out_k=torch.stack(cache.key_cache).numpy(),
+                        out_v=torch.stack(cache.value_cache).numpy())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the CAST checkout")
+    ap.add_argument("--only", default="", help="comma-separated subset of the files to write (by stem)")
     args = ap.parse_args()
     tree, verify, decode, tta = _import_reference(args.reference)
-    tree_cfg1(tree)
-    tree_cases(tree)
-    topk_vocab(tree)
-    attn_cfg1(tree, verify)
-    attn_ragged(tta)
-    walk(tree, decode)
+    want = set(x for x in args.only.split(",") if x)
+    run = lambda stem: not want or stem in want
+    if run("tree_cfg1"):
+        tree_cfg1(tree)
+    if run("tree_cases"):
+        tree_cases(tree)
+    if run("topk_vocab"):
+        topk_vocab(tree)
+    if run("attn_cfg1"):
+        attn_cfg1(tree, verify)
+    if run("attn_ragged"):
+        attn_ragged(tta)
+    if run("walk"):
+        walk(tree, decode)
+    if run("select"):
+        select(tree)
+    if run("append"):
+        append(importlib.import_module("cast_trees.serving"))
+    if run("gather"):
+        gather(verify)
     print("golden vectors written to", HERE)
 
 

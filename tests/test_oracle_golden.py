@@ -116,3 +116,45 @@ def test_walk_tree_greedy(golden):
         path, bonus = otree.walk_tree_greedy(g[f"c{c}_parent"], g[f"c{c}_token"], g[f"c{c}_logits"])
         assert path == g[f"c{c}_path"].tolist()
         assert bonus == int(g[f"c{c}_bonus"])
+
+
+def _forest(g, prefix):
+    cnt = g[prefix + "count"]
+    return [otree.Tree(g[prefix + "token"][b, :n], g[prefix + "depth"][b, :n], g[prefix + "parent"][b, :n],
+                       g[prefix + "score"][b, :n]) for b, n in enumerate(cnt)]
+
+
+@pytest.mark.parametrize("forest", ["rand", "ties", "same"])
+def test_select_global_topk(golden, forest):
+    g = golden("select.npz")
+    trees = _forest(g, f"{forest}_in_")
+    for total in g["totals"].tolist():
+        got = otree.select_global_topk(trees, total)
+        want = _forest(g, f"{forest}_t{total}_")
+        assert [len(t) for t in got] == [len(t) for t in want], total
+        for a, b in zip(got, want):
+            for f in ("token", "depth", "parent"):
+                assert np.array_equal(getattr(a, f), getattr(b, f)), (total, f)
+            assert np.array_equal(a.score, b.score)
+
+
+@pytest.mark.parametrize("case", ["inplace", "compact", "grow"])
+def test_append_store(golden, case):
+    from oracle import kv as okv
+    g = golden("append.npz")
+    keep = [[int(x) for x in row if x >= 0] for row in g[f"{case}_keep"]]
+    ks, vs, new_len = okv.append_store(list(g[f"{case}_in_k"]), list(g[f"{case}_in_v"]),
+                                       g[f"{case}_store_len"].tolist(), g[f"{case}_cu_q"].tolist(), keep,
+                                       g[f"{case}_accepted"].tolist(), g[f"{case}_rows"].tolist(),
+                                       list(g[f"{case}_pack_k"]), list(g[f"{case}_pack_v"]))
+    assert new_len == g[f"{case}_new_len"].tolist()
+    assert np.array_equal(np.stack(ks), g[f"{case}_out_k"])
+    assert np.array_equal(np.stack(vs), g[f"{case}_out_v"])
+
+
+def test_gather_cache(golden):
+    from oracle import kv as okv
+    g = golden("gather.npz")
+    ks, vs = okv.gather_cache(list(g["in_k"]), list(g["in_v"]), int(g["n_prefix"]), g["keep"].tolist())
+    assert np.array_equal(np.stack(ks), g["out_k"])
+    assert np.array_equal(np.stack(vs), g["out_v"])
