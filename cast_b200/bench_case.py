@@ -35,6 +35,8 @@ def main():
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--dtype", choices=["bf16", "fp16", "fp32"], default="bf16")
+    ap.add_argument("--graph", action="store_true",
+                    help="also time the calls replayed from a CUDA graph (device time without host overhead)")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[args.dtype]
@@ -110,7 +112,7 @@ def main():
         elif args.what == "select":
             cast_b200.select_global_topk_device(sel_src, 8 * w.B, pack_capacity=w.B * 9)
         elif args.what == "append":
-            cast_b200.append_store_inplace(bk, bv, sl_t, cu_q[:-1], walk_out.accepted, walk_out.keep, pk, pv)
+            cast_b200.append_store_inplace(bk, bv, sl_t, cu_q[:-1], walk_out.keep, walk_out.accepted, pk, pv)
         else:
             cast_b200.build_trees(idx, lp, budget, 8, max_budget=max(w.N), cu_q=cu_q, total_q=lay["total_q"])
 
@@ -126,9 +128,29 @@ def main():
         raise RuntimeError("device error")
     rec = {"what": args.what, "config": args.config, "batch": w.B,
            "us_per_launch": round(ev[0].elapsed_time(ev[1]) * 1e3 / args.iters, 1)}
+    if args.graph:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            once()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.iters):
+                once()
+        graph.replay()
+        torch.cuda.synchronize()
+        ev[0].record()
+        graph.replay()
+        ev[1].record()
+        torch.cuda.synchronize()
+        if _lib.device_error() != 0:
+            raise RuntimeError("device error")
+        rec["us_per_launch_graph"] = round(ev[0].elapsed_time(ev[1]) * 1e3 / args.iters, 1)
     if args.what in ("walk", "append"):
         acc = walk_out.accepted.cpu()
         rec["mean_accepted"] = round(float(acc.float().mean()), 2)
+        rec["max_accepted"] = int(acc.max())
         rec["rows_read"] = int(acc.sum())    # logits rows the walk read: one per accepted token
     print(json.dumps(rec))
 

@@ -543,8 +543,9 @@ int cast_tree_walk_greedy(const void* logits, int dtype, int64_t row_stride, int
   const bool vec = aligned(logits, 16) && (row_stride * es) % 16 == 0;
   const int sms = sm_count();
   if (sms <= 0) return CAST_ERR_DEVICE;
+  // one cluster per sequence, wide enough for about two CTAs per SM
   int cs = 1;
-  while (cs < 8 && (int64_t)B * cs < sms) cs *= 2;
+  while (cs < 8 && (int64_t)B * cs < 2 * sms) cs *= 2;
   walk::WalkArgs a{logits, row_stride, V, cu_q, pack_parent, pack_token, B, total_q, path_cap,
                    path, accepted, bonus, keep, tokens};
   cudaLaunchConfig_t cfg = {};
@@ -591,11 +592,16 @@ int cast_select_global_topk(const int32_t* token, const int32_t* depth, const in
   if ((const void*)out_token == token || (const void*)out_depth == depth || (const void*)out_parent == parent ||
       (const void*)out_score == score)
     return CAST_ERR_ALIGN;
-  sel::SelArgs a{token, depth, parent, score, count, B, max_nodes, total, out_token, out_depth, out_parent,
-                 out_score, out_count, cu_q, root_token, seq_len, pack_parent, pack_token, pack_pos, pack_capacity};
-  const size_t smem = (size_t)(2 * B + 1) * sizeof(int);
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(sel::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  // pooled keys go to shared memory when they fit beside the offset arrays
+  const size_t base_smem = (size_t)((3 * B + 1 + 1) & ~1) * sizeof(int);
+  const size_t key_smem = (size_t)B * max_nodes * sizeof(uint64_t);
+  const int cache_keys = base_smem + key_smem <= sel::MAX_DYN_SMEM ? 1 : 0;
+  sel::SelArgs a{token, depth, parent, score, count, B, max_nodes, cache_keys, total, out_token, out_depth,
+                 out_parent, out_score, out_count, cu_q, root_token, seq_len, pack_parent, pack_token, pack_pos,
+                 pack_capacity};
+  const size_t smem = base_smem + (cache_keys ? key_smem : 0);
+  // the static arrays already take ~37 KB, so any dynamic size needs the opt-in
+  if (cudaFuncSetAttribute(sel::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return CAST_ERR_LAUNCH;
   sel::select_kernel<<<1, sel::NT, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
@@ -633,10 +639,17 @@ int kv_gather(int n_layers, const void* const* src_kv, void* const* dst_kv, cons
         ly.pack[l][kv] = static_cast<const char*>(pack_kv[2 * (l0 + l) + kv]) + pack_offset_bytes;
       }
     a.L = nl;
-    dim3 grid(gx, (unsigned)(a.B_dst * a.H), (unsigned)nl);
-    if (p16) kvg::kv_gather_kernel<uint4><<<grid, kvg::NT, 0, st>>>(a, ly);
-    else if (p4) kvg::kv_gather_kernel<uint32_t><<<grid, kvg::NT, 0, st>>>(a, ly);
-    else kvg::kv_gather_kernel<uint16_t><<<grid, kvg::NT, 0, st>>>(a, ly);
+    if (a.append_only) {
+      dim3 grid((unsigned)a.B_dst, (unsigned)((nl + kvg::LAYERS_PER_CTA - 1) / kvg::LAYERS_PER_CTA));
+      if (p16) kvg::kv_append_kernel<uint4><<<grid, kvg::NT, 0, st>>>(a, ly);
+      else if (p4) kvg::kv_append_kernel<uint32_t><<<grid, kvg::NT, 0, st>>>(a, ly);
+      else kvg::kv_append_kernel<uint16_t><<<grid, kvg::NT, 0, st>>>(a, ly);
+    } else {
+      dim3 grid(gx, (unsigned)(a.B_dst * a.H), (unsigned)nl);
+      if (p16) kvg::kv_gather_kernel<uint4><<<grid, kvg::NT, 0, st>>>(a, ly);
+      else if (p4) kvg::kv_gather_kernel<uint32_t><<<grid, kvg::NT, 0, st>>>(a, ly);
+      else kvg::kv_gather_kernel<uint16_t><<<grid, kvg::NT, 0, st>>>(a, ly);
+    }
     if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
   }
   return CAST_OK;

@@ -52,8 +52,9 @@ def append_store(buf_k, buf_v, store_len, cu_q, keep, accepted, rows, pack_k, pa
     surviving requests; pack_k / pack_v: per-layer pass K/V [H, total_q, D]
     (the hook's key[0] / value[0]). Returns (buf_k, buf_v, new_len) exactly as
     the reference: the same tensors appended in place when no request leaves
-    and no store grows, else new stores (rows compacted in `rows` order,
-    capacity max(max(new_len), 2 * cap) when it grows, tails zero).
+    and no store grows, else new stores (whole store rows gathered in `rows`
+    order, capacity max(max(new_len), 2 * cap) when it grows with the new
+    rows zero, then the appended rows written).
     """
     L = len(buf_k)
     new_len = [store_len[b] + accepted[b] for b in rows]
@@ -112,6 +113,8 @@ def append_store_inplace(buf_k, buf_v, store_len, cu_q, keep, accepted, pack_k, 
     B, H, cap, D = buf_k[0].shape
     i32 = lambda t: torch.as_tensor(t, device=dev).to(torch.int32).contiguous()
     sl, cq, acc, kp = i32(store_len), i32(cu_q), i32(accepted), i32(keep)
+    if kp.dim() != 2 or kp.shape[0] != B or sl.numel() != B or cq.numel() < B or acc.numel() != B:
+        raise ValueError("append_store_inplace: store_len / cu_q / accepted need B entries and keep [B, w]")
     src = _pairs(buf_k, buf_v)
     p0 = pack_k[0]
     st = _i64(*buf_k[0].stride()[:3])

@@ -67,7 +67,7 @@ enum cast_status {
 #define CAST_MAX_PACK 1024    /* largest pack (1 + N) the attention kernels accept */
 #define CAST_MAX_TOPK 24      /* largest k of block_topk / build_tree */
 #define CAST_MAX_DEPTH 64     /* largest L of build_tree */
-#define CAST_MAX_SELECT_TREES 16384  /* largest forest of cast_select_global_topk */
+#define CAST_MAX_SELECT_TREES 12288  /* largest forest of cast_select_global_topk */
 #define CAST_MAX_SELECT_NODES 1024   /* largest tree (row width) of cast_select_global_topk */
 
 /* Human-readable text for a status code (never NULL). */
@@ -288,10 +288,12 @@ int cast_select_global_topk(const int32_t* token, const int32_t* depth, const in
  * batch, head, row in elements; dim stride 1); pack K/V are the verify pass's
  * [H, total_q, D] per-layer tensors (pack_strides = batch (0), head, row).
  * For destination row nb (source row b = rows[nb], or nb when rows is NULL),
- * head h, layer l: rows [0, store_len[b]) copy the source store, rows
- * store_len[b] + j (j < accepted[b]) take pack row cu_q[b] + keep[b * keep_stride + j],
- * and rows up to dst_cap are zeroed. append_only = 1 writes only the appended
- * rows of a store in place (dst_kv == src_kv, rows NULL, same shape).
+ * head h, layer l: rows store_len[b] + j (j < accepted[b]) take pack row
+ * cu_q[b] + keep[b * keep_stride + j]; every other row below src_cap copies
+ * source row b and rows from src_cap to dst_cap are zero (the reference's
+ * gather of whole store rows, zero growth, then the append). append_only = 1
+ * writes only the appended rows of a store in place (dst_kv == src_kv, rows
+ * NULL, same shape).
  */
 int cast_append_store(int n_layers, const void* const* src_kv, void* const* dst_kv, const void* const* pack_kv,
                       int elem_bytes, int H, int D, int B_src, int64_t src_cap, const int64_t* src_strides,

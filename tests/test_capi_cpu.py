@@ -82,3 +82,43 @@ def test_tree_argument_checks(L):
     assert L.cast_build_tree(p, p, 1, 15, 8, 8, p, 10, p, p, p, p, p, nul, p, nul, nul, nul, nul, None) == -1
     assert L.cast_build_tree(p, p, 1, 15, 8, 8, p, 10, p, p, p, p, p, p, nul, nul, p, nul, nul, None) == -1
     assert L.cast_build_tree(p, p, 0, 15, 8, 8, p, 10, p, p, p, p, p, nul, nul, nul, nul, nul, nul, None) == 0
+
+
+def test_walk_select_append_gather_argument_checks(L):
+    # argument errors come back before any CUDA call
+    p = 1 << 12
+    walk = lambda **o: L.cast_tree_walk_greedy(*dict(dict(
+        logits=p, dtype=1, row_stride=64, V=64, cu_q=p, par=p, tok=p, B=2, total_q=8, cap=4, path=p, acc=p,
+        bonus=p, keep=None, tokens=None, stream=None), **o).values())
+    assert walk(dtype=9) == -3
+    assert walk(V=0) == -2 and walk(row_stride=32) == -2 and walk(cap=0) == -2
+    assert walk(logits=None) == -1 and walk(bonus=None) == -1
+    assert walk(B=0) == 0
+    sel = lambda **o: L.cast_select_global_topk(*dict(dict(
+        tok=p, dep=p, par=p, sc=p, cnt=p, B=4, mb=48, total=16, otok=p * 2, odep=p * 2, opar=p * 2, osc=p * 2,
+        ocnt=p * 2, cu_q=None, rt=None, sl=None, pp=None, pt=None, ppos=None, cap=0, stream=None), **o).values())
+    assert sel(mb=0) == -2 and sel(mb=2048) == -2 and sel(B=100000) == -2
+    assert sel(tok=None) == -1 and sel(ocnt=None) == -1
+    assert sel(pp=p) == -1                        # pack arrays need cu_q
+    assert sel(cu_q=p, pt=p) == -1                # pack tokens need root tokens
+    assert sel(otok=p) == -7                      # outputs may not be the inputs
+    assert sel(B=0) == 0
+    ptrs = (ctypes.c_void_p * 2)(p, p)
+    st = (ctypes.c_int64 * 3)(1024, 128, 1)
+    app = lambda **o: L.cast_append_store(*dict(dict(
+        L=1, src=ptrs, dst=ptrs, pack=ptrs, es=2, H=8, D=128, Bs=2, scap=16, sst=st, Bd=2, dcap=16, dst_st=st,
+        prow=8, pst=st, rows=None, sl=p, acc=p, keep=p, ks=4, cu=p, app=1, stream=None), **o).values())
+    assert app(es=3) == -3
+    assert app(H=0) == -2 and app(Bd=40000) == -2
+    assert app(keep=None) == -1
+    assert app(rows=p) == -2                      # append in place takes no row map
+    other = (ctypes.c_void_p * 2)(p * 2, p * 2)
+    assert app(dst=other) == -2                   # ... and writes the stores it reads
+    assert app(L=0) == 0 and app(Bd=0) == 0
+    gat = lambda **o: L.cast_gather_cache(*dict(dict(
+        L=1, src=ptrs, dst=other, es=2, B=1, H=8, D=128, slen=20, sst=st, dst_st=st, npre=12, keep=p, nk=3,
+        stream=None), **o).values())
+    assert gat(es=8) == -3
+    assert gat(npre=30) == -2 and gat(nk=-1) == -2
+    assert gat(keep=None) == -1
+    assert gat(B=0) == 0 and gat(npre=0, nk=0) == 0

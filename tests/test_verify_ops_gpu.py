@@ -254,7 +254,7 @@ def test_append_store_inplace_from_walk(cuda):
     keep = [row[:a] for row, a in zip(w.keep.cpu().tolist(), acc)]
     rk, rv, _ = okv.append_store(host(bufk), host(bufv), sl.cpu().tolist(), cu_q.tolist(), keep, acc,
                                  list(range(B)), host(pk), host(pv))
-    cast_b200.append_store_inplace(bufk, bufv, sl, cu_t[:-1], w.accepted, w.keep, pk, pv)
+    cast_b200.append_store_inplace(bufk, bufv, sl, cu_t[:-1], w.keep, w.accepted, pk, pv)
     assert _lib.device_error() == 0
     for li in range(L):
         assert np.array_equal(bufk[li].float().cpu().numpy(), rk[li])
