@@ -436,6 +436,8 @@ def run_reference(args):
 
 
 def main():
+    # NCCL's own prints (its version line) go to stderr: stdout carries the one JSON line
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
