@@ -715,8 +715,7 @@ int cast_gather_cache(int n_layers, const void* const* src_kv, void* const* dst_
   a.dst_sb = dst_strides[0] * e; a.dst_sh = dst_strides[1] * e; a.dst_sr = dst_strides[2] * e;
   a.pk_sb = a.src_sb; a.pk_sh = a.src_sh; a.pk_st = a.src_sr;
   a.rows = nullptr; a.store_len = nullptr; a.accepted = nullptr; a.s_const = n_prefix; a.a_const = n_keep;
-  static const int32_t kNoKeep = 0;
-  a.keep = n_keep > 0 ? keep : &kNoKeep;   // never read when n_keep == 0
+  a.keep = n_keep > 0 ? keep : nullptr;   // with no kept rows the kernel never reads it
   a.keep_stride = 0; a.cu_q = nullptr;
   return kv_gather(n_layers, src_kv, dst_kv, src_kv, (int64_t)n_prefix * a.src_sr, a, a.dst_cap,
                    static_cast<cudaStream_t>(stream));
