@@ -205,10 +205,10 @@ def select_global_topk(trees, total):
     by (-score, request, node) are kept, in node order, parents renumbered);
     computed on the GPU.
     """
-    dev = _cuda_device()
     B = len(trees)
     if B == 0:
         return []
+    dev = _cuda_device()
     mb = max(1, max(len(t) for t in trees))
     tok = np.zeros((B, mb), dtype=np.int32)
     dep = np.zeros((B, mb), dtype=np.int32)
