@@ -61,6 +61,7 @@ struct Bars {
   uint64_t k_full[NST], k_empty[NST], v_full[NST], v_empty[NST];
   uint64_t s_full[QT], p_full[QT];
   uint64_t o_full;
+  uint64_t comb;   // dual mode: the odd-tile half's (m, l) are in shared memory
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -101,6 +102,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   __shared__ __align__(8) Bars bars;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
+  __shared__ float comb_m[BM], comb_l[BM];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.y / p.H_kv, h = blockIdx.y % p.H_kv;
@@ -153,6 +155,10 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
     }
   };
   const bool has_pack_tile = STORE ? (t_begin + n_kt > nt_pre) : (k_end > m.S);
+  // A CTA with a single query tile runs it as two interleaved key streams (even key tiles on
+  // S_0/O_0, odd ones on S_1/O_1, each with its own softmax warpgroup) and merges the two
+  // partial softmaxes at the end: the same overlap as two query tiles, on half the key tiles each.
+  const bool dual = n_qt == 1 && n_kt >= 2;
   volatile int* abort_flag = &abort_sh;
 
   if (tid == 0) {
@@ -168,6 +174,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       mbar_init(smem_u32(&bars.p_full[q]), BM);
     }
     mbar_init(smem_u32(&bars.o_full), 1);
+    mbar_init(smem_u32(&bars.comb), BM);
     abort_sh = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -251,8 +258,9 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
     const uint64_t dQ0 = desc_kmajor(sQ), dQ1 = desc_kmajor(sQ + TILE_BYTES);
     const uint64_t dK0 = desc_kmajor(sK), dK1 = desc_kmajor(sK + TILE_BYTES);
     const uint64_t dV0 = desc_mnmajor(sV, HALF_BYTES), dV1 = desc_mnmajor(sV + TILE_BYTES, HALF_BYTES);
-    auto qk = [&](int q, int j) {
-      const uint64_t a = q ? dQ1 : dQ0, b = (j % NST) ? dK1 : dK0;
+    // S_q = Q_qa K(slot s)^T
+    auto qk_ = [&](int q, int qa, int s) {
+      const uint64_t a = qa ? dQ1 : dQ0, b = s ? dK1 : dK0;
       if (elect_one()) {
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
@@ -262,16 +270,19 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       }
       __syncwarp();
     };
-    auto pv = [&](int q, int j) {
-      const uint64_t b = (j % NST) ? dV1 : dV0;
+    // O_q (+)= P_q V(slot s); `first` starts the accumulator
+    auto pv_ = [&](int q, int s, bool first) {
+      const uint64_t b = s ? dV1 : dV0;
       if (elect_one()) {
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k)
           mma_ts(tmem + 256 + q * 128, tmem + q * 128 + k * 8, b + (uint64_t)((k * 2048) >> 4), idesc_pv,
-                 (j > 0 || k > 0) ? 1u : 0u);
+                 (!first || k > 0) ? 1u : 0u);
       }
       __syncwarp();
     };
+    auto qk = [&](int q, int j) { qk_(q, q, j % NST); };
+    auto pv = [&](int q, int j) { pv_(q, j % NST, j == 0); };
     auto commit = [&](uint64_t& bar) {
       if (elect_one()) mma_commit(smem_u32(&bar));
       __syncwarp();
@@ -279,8 +290,74 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
     auto wait_all = [&](uint64_t& bar, uint32_t parity) {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(&bar), parity, abort_flag));
     };
+    // Store mode: the last prefix tile also holds store rows past the prefix; their scores
+    // are masked, but 0 x (a non-finite stale value) would still poison P V, so those V rows
+    // are zeroed (whole 128-byte rows: the swizzle only permutes inside a row).
+    auto zero_tail = [&](int j, int s) {
+      if constexpr (STORE) {
+        int n0, klim;
+        tile_keys(j, n0, klim);
+        if (n0 < m.S && n0 + BN > m.S) {
+          uint8_t* vt = smem + SMEM_V + s * TILE_BYTES;
+          for (int e = lane; e < (n0 + BN - m.S) * 16; e += 32) {
+            const int r = m.S - n0 + (e >> 4), c = e & 15;
+            *reinterpret_cast<uint4*>(vt + (c >> 3) * HALF_BYTES + r * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+      }
+    };
     bool ok = wait_all(bars.q_full, 0);
-    for (int j = 0; ok && j < n_kt; ++j) {
+    if (dual) {
+      // step i: QK of key tile 2i on S_0, PV of key tile 2i-1 (S_1), QK of key tile 2i+1 on S_1,
+      // PV of key tile 2i (S_0); both QKs read query tile 0
+      const int n_pairs = (n_kt + 1) / 2;
+      for (int i = 0; ok && i < n_pairs; ++i) {
+        const int j0 = 2 * i, j1 = 2 * i + 1;
+        const int s0 = j0 % NST, s1 = j1 % NST;
+        if (!(ok = wait_all(bars.k_full[s0], (uint32_t)(j0 / NST) & 1))) break;
+        fence_after_sync();
+        qk_(0, 0, s0);
+        commit(bars.s_full[0]);
+        commit(bars.k_empty[s0]);
+        if (i > 0) {
+          const int jp = j1 - 2, sp = jp % NST;
+          if (!(ok = wait_all(bars.v_full[sp], (uint32_t)(jp / NST) & 1))) break;
+          zero_tail(jp, sp);
+          if (!(ok = wait_all(bars.p_full[1], (uint32_t)(i - 1) & 1))) break;
+          fence_after_sync();
+          pv_(1, sp, i == 1);
+          commit(bars.v_empty[sp]);
+        }
+        if (j1 < n_kt) {
+          if (!(ok = wait_all(bars.k_full[s1], (uint32_t)(j1 / NST) & 1))) break;
+          fence_after_sync();
+          qk_(1, 0, s1);
+          commit(bars.s_full[1]);
+          commit(bars.k_empty[s1]);
+        }
+        if (!(ok = wait_all(bars.v_full[s0], (uint32_t)(j0 / NST) & 1))) break;
+        zero_tail(j0, s0);
+        if (!(ok = wait_all(bars.p_full[0], (uint32_t)i & 1))) break;
+        fence_after_sync();
+        pv_(0, s0, i == 0);
+        commit(bars.v_empty[s0]);
+      }
+      const int jl = 2 * n_pairs - 1;   // the last odd key tile, if there is one
+      if (ok && jl < n_kt) {
+        const int sl = jl % NST;
+        if (wait_all(bars.v_full[sl], (uint32_t)(jl / NST) & 1)) {
+          zero_tail(jl, sl);
+          if (wait_all(bars.p_full[1], (uint32_t)(n_pairs - 1) & 1)) {
+            fence_after_sync();
+            pv_(1, sl, n_pairs == 1);
+            commit(bars.v_empty[sl]);
+          }
+        }
+      }
+    }
+    for (int j = 0; ok && !dual && j < n_kt; ++j) {
       const int s = j % NST;
       const uint32_t ph = (uint32_t)(j / NST) & 1;
       if (!(ok = wait_all(bars.k_full[s], ph))) break;
@@ -299,28 +376,13 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       }
       commit(bars.k_empty[s]);
       if (!(ok = wait_all(bars.v_full[s], ph))) break;
-      if constexpr (STORE) {
-        // The last prefix tile also holds store rows past the prefix: their scores are
-        // masked, but 0 x (a non-finite stale value) would still poison P V, so those
-        // V rows are zeroed (whole 128-byte rows: the swizzle only permutes inside a row).
-        int n0, klim;
-        tile_keys(j, n0, klim);
-        if (n0 < m.S && n0 + BN > m.S) {
-          uint8_t* vt = smem + SMEM_V + s * TILE_BYTES;
-          for (int e = lane; e < (n0 + BN - m.S) * 16; e += 32) {
-            const int r = m.S - n0 + (e >> 4), c = e & 15;
-            *reinterpret_cast<uint4*>(vt + (c >> 3) * HALF_BYTES + r * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-        }
-      }
+      zero_tail(j, s);
       if (!(ok = wait_all(bars.p_full[0], (uint32_t)j & 1))) break;
       fence_after_sync();
       pv(0, j);
       if (n_qt == 1) commit(bars.v_empty[s]);
     }
-    if (ok && n_qt == 2) {
+    if (ok && !dual && n_qt == 2) {
       if (wait_all(bars.p_full[1], (uint32_t)(n_kt - 1) & 1)) {
         fence_after_sync();
         pv(1, n_kt - 1);
@@ -334,11 +396,13 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
     // ------------------------------------------------------------ softmax / epilogue
     const int q = (warp - 4) >> 2;
     const int t = tid - 128 - q * BM;  // == TMEM lane
-    if (q < n_qt) {
+    if (q < n_qt || dual) {
       const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
       const uint32_t S_t = tmem + lane_off + q * 128;
       const uint32_t O_t = tmem + lane_off + 256 + q * 128;
-      const int r = r_base + q * BM + t;
+      const int r = r_base + (dual ? 0 : q * BM) + t;
+      // key tiles of this warpgroup: all of them, or every other one in dual mode
+      const int n_steps = dual ? (n_kt + 1 - q) / 2 : n_kt;
       const int li = min(r / G, m.P - 1) - i_lo;
       const uint64_t* anc = sAnc + (size_t)li * p.W;
       const float c = p.scale_log2;
@@ -349,12 +413,12 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       // kept warp-uniform (waits are followed by a warp vote, per-row choices
       // are made with per-lane values inside uniform branches).
       uint32_t sv[BN];
-      for (int j = 0; j < n_kt; ++j) {
+      for (int j = 0; j < n_steps; ++j) {
         ok = mbar_wait(smem_u32(&bars.s_full[q]), (uint32_t)j & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         fence_after_sync();
         int n0, klim;
-        tile_keys(j, n0, klim);
+        tile_keys(dual ? 2 * j + q : j, n0, klim);
         const bool full = (n0 + BN <= m.S) && (n0 + BN <= klim);
         // visibility bits of the 128 keys (only tiles that reach the pack or the chunk end)
         auto mask32 = [&](int nb) -> uint32_t {
@@ -437,6 +501,40 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       bool done = mbar_wait(smem_u32(&bars.o_full), 0, ok ? abort_flag : nullptr);
       done = __all_sync(0xffffffffu, done && ok);
       fence_after_sync();
+      // dual mode: the odd-tile warpgroup hands its (m, l) over; the even one merges the two
+      // partials (O_1 sits in the same TMEM lanes, columns 384..511) and writes the rows
+      float a0 = 1.f, a1 = 0.f;
+      if (dual) {
+        if (q == 1) {
+          comb_m[t] = m_ref;
+          comb_l[t] = l;
+          mbar_arrive(smem_u32(&bars.comb));
+          done = false;
+        } else {
+          done = __all_sync(0xffffffffu, done && mbar_wait(smem_u32(&bars.comb), 0, abort_flag));
+          if (done) {
+            const float m1 = comb_m[t], l1 = comb_l[t];
+            const float mx = fmaxf(m_ref, m1);
+            a0 = m_ref == -INFINITY ? 0.f : ex2(m_ref - mx);
+            a1 = m1 == -INFINITY ? 0.f : ex2(m1 - mx);
+            l = l * a0 + l1 * a1;
+            m_ref = mx;
+          }
+        }
+      }
+      const uint32_t O1_t = tmem + lane_off + 256 + 128;
+      auto load_o = [&](int cc) {
+        tmem_ld32(O_t + cc * 32, v);
+        tmem_ld_wait();
+        if (dual) {
+          uint32_t w[32];
+          tmem_ld32(O1_t + cc * 32, w);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            v[i] = __float_as_uint(__uint_as_float(v[i]) * a0 + __uint_as_float(w[i]) * a1);
+        }
+      };
       if (done) {
         const bool store = r < rows;
         const int i = min(r / G, m.P - 1), hq = h * G + r % G;
@@ -447,8 +545,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
           T* out = static_cast<T*>(p.out) + tq * p.so_m + (int64_t)hq * p.so_h;
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
-            tmem_ld32(O_t + cc * 32, v);
-            tmem_ld_wait();
+            load_o(cc);
             uint32_t pk[16];
 #pragma unroll
             for (int i2 = 0; i2 < 16; ++i2)
@@ -464,8 +561,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
           float* O = p.ws_o + slot * D;
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
-            tmem_ld32(O_t + cc * 32, v);
-            tmem_ld_wait();
+            load_o(cc);
             if (store) {
               float4* dst = reinterpret_cast<float4*>(O + cc * 32);
 #pragma unroll
