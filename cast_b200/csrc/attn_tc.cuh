@@ -18,6 +18,9 @@
 //               rescale of O (only when the max grew by more than 2^8), then
 //               P = exp2(S*c - m) rounded to 16 bits and stored into the first
 //               64 columns of S (tcgen05.st), which the PV MMA reads.
+// A CTA with one query tile and two or more key tiles runs "dual": its even key
+// tiles go through S_0/O_0 (warps 4-7) and its odd ones through S_1/O_1 (warps
+// 8-11), both on query tile 0, and the epilogue merges the two partial softmaxes.
 // Tensor memory (512 columns): S_0, S_1 (128 fp32 columns each), O_0, O_1.
 // Visibility: keys < S_b always; pack key S_b + j iff bit j of the row token's
 // ancestor bitset (shared memory; built from `parent` or copied); keys past
