@@ -248,3 +248,40 @@ def test_tensor_core_and_cuda_core_agree(cuda):
     assert (a.float().cpu() - ref).abs().max().item() < 2e-2
     assert (b.float().cpu() - ref).abs().max().item() < 2e-2
     assert (a.float() - b.float()).abs().max().item() < 2e-2
+
+
+def _scenario(S_list, P_list, Hq=32, Hkv=8, D=128, seed=5):
+    """Explicit prefix / pack lengths; random pack trees; q/k/v ~ N(0, 1)."""
+    g = torch.Generator().manual_seed(seed)
+    rng = np.random.default_rng(seed)
+    parents = []
+    for P in P_list:
+        parents += [-1] + [int(rng.integers(0, i)) for i in range(1, P)]
+    cu_q = np.concatenate([[0], np.cumsum(P_list)]).astype(np.int32)
+    cu_kv = np.concatenate([[0], np.cumsum(np.array(S_list) + np.array(P_list))]).astype(np.int32)
+    return dict(q=torch.randn(int(cu_q[-1]), Hq, D, generator=g), k=torch.randn(int(cu_kv[-1]), Hkv, D, generator=g),
+                v=torch.randn(int(cu_kv[-1]), Hkv, D, generator=g), cu_q=torch.from_numpy(cu_q),
+                cu_kv=torch.from_numpy(cu_kv), prefix=np.array(S_list, np.int32), pack=np.array(P_list, np.int32),
+                parent=np.array(parents, np.int32))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_single_tile_ctas_two_key_streams(cuda, dtype):
+    # one 128-row query tile with 2, 3, 5, 8 and 1 key tiles; a 280-row head group whose second block
+    # holds one tile; a row whose only visible key is its own root (S = 0)
+    sc = _scenario([200, 300, 600, 1000, 50, 500, 0], [20, 30, 7, 24, 10, 70, 3])
+    got = _run(sc, dtype, cuda).float().cpu()
+    err = (got - _oracle(sc, dtype)).abs().max().item()
+    assert err < TOL[dtype], err
+
+
+def test_single_tile_ctas_with_key_splits(cuda):
+    # two long prefixes, small packs: the launch splits the keys and every chunk runs two key streams
+    sc = _scenario([30000, 17001], [9, 2], seed=6)
+    q16 = sc["q"].to(cuda, torch.bfloat16)
+    kernel, n_split, _ = cast_b200.attention_plan(q16, sc["k"].to(cuda, torch.bfloat16),
+                                                 sc["v"].to(cuda, torch.bfloat16), torch.empty_like(q16), 2, 9, 30009)
+    assert kernel == "tcgen05" and n_split > 1
+    got = _run(sc, torch.bfloat16, cuda).float().cpu()
+    err = (got - _oracle(sc, torch.bfloat16)).abs().max().item()
+    assert err < TOL[torch.bfloat16], err
