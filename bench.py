@@ -349,7 +349,7 @@ def run_cast(args):
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(result)
 
 
 def _cpu_sample(w, ids):
@@ -419,7 +419,7 @@ def run_reference(args):
             flops += fl * args.layers
     tot = sum(times)
     value = flops / tot / 1e12
-    print(json.dumps({
+    emit({
         "metric": METRIC, "impl": "reference", "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * tot / args.steps, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 inputs, fp32 compute",
@@ -432,12 +432,24 @@ def run_reference(args):
                          "kind": "port", "sample": f"{n} config-3 sequences per step; the reference is Python: "
                                                    f"its numpy tree builder and its fp32 masked-softmax attention"},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
+
+
+_JSON_FD = None
+
+
+def emit(obj):
+    """The one JSON line, on the real stdout (fd 1 itself is pointed at stderr in main())."""
+    os.write(_JSON_FD if _JSON_FD is not None else 1, (json.dumps(obj) + "\n").encode())
 
 
 def main():
-    # NCCL's own prints (its version line) go to stderr: stdout carries the one JSON line
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    global _JSON_FD
+    # whatever the libraries print on stdout (NCCL's version line, for one) goes to stderr;
+    # stdout carries only the JSON line
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
