@@ -343,6 +343,7 @@ def run_cast(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    result["verify_round_rows"] = round_rows(st, trees, w, dev)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(w, trees, args)
     if world > 1:
@@ -350,6 +351,74 @@ def run_cast(args):
         dist.destroy_process_group()
     if rank == 0:
         emit(result)
+
+
+def round_rows(st, trees, w, dev, iters=10):
+    """Per-call device time of the verify-round steps after attention, on this rank's batch.
+
+    walk: greedy walk over synthetic bf16 target logits [total_q, V] that follow each tree's
+    first child with probability 3/4; select: select_global_topk_device keeping 48 nodes per
+    request; append: the walk's accepted rows into 32 layers of per-request stores in place
+    (the kernel's work depends only on the appended rows, so the stores hold no prefix here).
+    CUDA events around `iters` eager calls each.
+    """
+    try:
+        import cast_b200
+        lay = st.lay
+        gen = torch.Generator(device=dev).manual_seed(7)
+        V = w.V
+        tl = torch.empty((lay["total_q"], V), dtype=torch.bfloat16, device=dev)
+        tl.normal_(generator=gen)
+        pp = trees.pack_parent
+        ptok = torch.where(pp >= 0, torch.randint(0, V, pp.shape, device=dev, dtype=torch.int32, generator=gen),
+                           torch.zeros_like(pp))
+        rows = torch.arange(lay["total_q"], device=dev)
+        q0 = torch.repeat_interleave(st.cu_q[:-1].long(), st.pack.long())
+        par_abs = torch.where(pp >= 0, q0 + pp.long(), torch.full_like(q0, -1))
+        big = torch.iinfo(torch.int64).max
+        first = torch.full((lay["total_q"],), big, dtype=torch.int64, device=dev)
+        child = rows[par_abs >= 0]
+        first.scatter_reduce_(0, par_abs[child], child, reduce="amin")
+        has = (first < big) & (torch.rand(first.shape, generator=gen, device=dev) < 0.75)
+        tl[rows[has], ptok[first[has]].long()] = 50.0
+        cap = lay["max_pack"] - 1
+        walk = cast_b200.walk_trees_greedy(tl, st.cu_q, pp, ptok, cap)
+        n_layers = 32
+        mk = lambda: torch.zeros((w.B, w.H_kv, 32, w.D), dtype=torch.bfloat16, device=dev)
+        bk, bv = [mk() for _ in range(n_layers)], [mk() for _ in range(n_layers)]
+        pk = [torch.randn((w.H_kv, lay["total_q"], w.D), device=dev).to(torch.bfloat16) for _ in range(n_layers)]
+        zero = torch.zeros(w.B, dtype=torch.int32, device=dev)
+
+        def timed(fn):
+            fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return round(e0.elapsed_time(e1) * 1e3 / iters, 1)
+
+        res = {
+            "walk_us": timed(lambda: cast_b200.walk_trees_greedy(tl, st.cu_q, pp, ptok, cap, out=walk)),
+            "select_us": timed(lambda: cast_b200.select_global_topk_device(trees, 48 * w.B,
+                                                                           pack_capacity=49 * w.B)),
+            "append_us": timed(lambda: cast_b200.append_store_inplace(bk, bv, zero, st.cu_q[:-1], walk.keep,
+                                                                      walk.accepted, pk, pk)),
+        }
+        acc = walk.accepted.float()
+        res["mean_accepted"] = round(float(acc.mean()), 2)
+        res["rows_walked"] = int(acc.sum())
+        res["note"] = (f"{w.B} requests, V={V} bf16 target logits, select keeps 48 of {trees.token.shape[1]} "
+                       f"nodes per request, append covers {n_layers} layers x K,V; eager calls (host time "
+                       f"included), device-only times in profiles/")
+        from cast_b200 import _lib
+        if _lib.device_error() != 0:
+            res["error"] = "device error"
+        return res
+    except Exception as e:   # the round's steps are reported beside the metric, never instead of it
+        return {"error": f"{type(e).__name__}: {e}"}
 
 
 def _cpu_sample(w, ids):
