@@ -387,6 +387,7 @@ def round_rows(st, trees, w, dev, iters=10):
         mk = lambda: torch.zeros((w.B, w.H_kv, 32, w.D), dtype=torch.bfloat16, device=dev)
         bk, bv = [mk() for _ in range(n_layers)], [mk() for _ in range(n_layers)]
         pk = [torch.randn((w.H_kv, lay["total_q"], w.D), device=dev).to(torch.bfloat16) for _ in range(n_layers)]
+        pv = [torch.randn((w.H_kv, lay["total_q"], w.D), device=dev).to(torch.bfloat16) for _ in range(n_layers)]
         zero = torch.zeros(w.B, dtype=torch.int32, device=dev)
 
         def timed(fn):
@@ -405,7 +406,7 @@ def round_rows(st, trees, w, dev, iters=10):
             "select_us": timed(lambda: cast_b200.select_global_topk_device(trees, 48 * w.B,
                                                                            pack_capacity=49 * w.B)),
             "append_us": timed(lambda: cast_b200.append_store_inplace(bk, bv, zero, st.cu_q[:-1], walk.keep,
-                                                                      walk.accepted, pk, pk)),
+                                                                      walk.accepted, pk, pv)),
         }
         acc = walk.accepted.float()
         res["mean_accepted"] = round(float(acc.mean()), 2)
