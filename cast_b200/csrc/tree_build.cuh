@@ -152,6 +152,9 @@ __device__ __forceinline__ void scan_row(const double* x, int64_t V, F&& f) {
   }
 }
 
+template <int KC>
+__device__ __forceinline__ void merge_warp_lists(double* s_cx, int* s_ci, double* s_out_x, int* s_out_i);
+
 // Merges every thread's sorted list into s_out_* (the CTA's KC best, best first).
 template <int KC, int TLN>
 __device__ __forceinline__ void merge_lists(CandList<TLN>& cl, double* s_cx, int* s_ci, double* s_out_x,
@@ -172,6 +175,14 @@ __device__ __forceinline__ void merge_lists(CandList<TLN>& cl, double* s_cx, int
     if (lane == bl && bi >= 0) cl.pop_front();
     if (lane == 0) { s_cx[warp * KC + rnd] = bx; s_ci[warp * KC + rnd] = bi; }
   }
+  merge_warp_lists<KC>(s_cx, s_ci, s_out_x, s_out_i);
+}
+
+// CTA level: the KC best of the NW warp lists in s_cx / s_ci (index -1 = empty) into s_out_*.
+template <int KC>
+__device__ __forceinline__ void merge_warp_lists(double* s_cx, int* s_ci, double* s_out_x, int* s_out_i) {
+  using namespace topk;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __syncthreads();
   if (warp == 0) {                            // CTA level, over the NW warp lists
     for (int rnd = 0; rnd < KC; ++rnd) {
@@ -198,6 +209,68 @@ __device__ __forceinline__ void merge_lists(CandList<TLN>& cl, double* s_cx, int
   __syncthreads();
 }
 
+// Warp-level candidate set of the fast path: the warp's KC best (x desc, index
+// asc) seen so far live in a shared-memory buffer behind a threshold (the KC-th
+// of them); an element enters the buffer only if it beats the threshold, which
+// after the first few hundred elements is rare, so the common per-element cost
+// is one comparison and a ballot. When the buffer passes CAP - 32 entries it is
+// cut back to its KC best.
+namespace topk {
+constexpr int CAP = 64;
+}
+
+template <int KC>
+struct WarpCands {
+  double* x;   // [CAP] of this warp
+  int* i;
+  int n;       // entries held (warp-uniform)
+  double tx;   // threshold: the KC-th best held (valid once n >= KC after a cut)
+  int ti;
+  bool full;
+
+  // Keeps the KC best of the n entries, in order, and sets the threshold.
+  __device__ __forceinline__ void cut() {
+    const int lane = threadIdx.x & 31;
+    __syncwarp();
+    double vx[topk::CAP / 32];
+    int vi[topk::CAP / 32], rk[topk::CAP / 32];
+#pragma unroll
+    for (int u = 0; u < topk::CAP / 32; ++u) {
+      const int e = lane + 32 * u;
+      vx[u] = e < n ? x[e] : -INFINITY;
+      vi[u] = e < n ? i[e] : -1;
+      int r = 0;
+      if (e < n)
+        for (int f = 0; f < n; ++f) r += cand_before(x[f], i[f], vx[u], vi[u]);
+      rk[u] = r;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < topk::CAP / 32; ++u)
+      if (vi[u] >= 0 && rk[u] < KC) { x[rk[u]] = vx[u]; i[rk[u]] = vi[u]; }
+    __syncwarp();
+    n = min(n, KC);
+    full = n >= KC;
+    if (full) { tx = x[KC - 1]; ti = i[KC - 1]; }
+  }
+
+  // One element per lane (valid = inside the row); every lane of the warp calls it.
+  __device__ __forceinline__ void offer(double v, int j, bool valid) {
+    const int lane = threadIdx.x & 31;
+    const bool pass = (v > tx && valid) || (valid && (!full || (v == tx && j < ti)));
+    const unsigned mask = __ballot_sync(0xffffffffu, pass);
+    if (mask) {
+      if (pass) {
+        const int pos = n + __popc(mask & ((1u << lane) - 1u));
+        x[pos] = v;
+        i[pos] = j;
+      }
+      n += __popc(mask);
+      if (n > topk::CAP - 32) cut();
+    }
+  }
+};
+
 template <int KC, bool VEC2>
 __global__ void __launch_bounds__(topk::NT)
 block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
@@ -208,25 +281,89 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
   __shared__ int s_ci[NW * KC];
   __shared__ double s_fx[KC], s_flp[KC];
   __shared__ int s_fi[KC];
+  __shared__ double w_x[NW][CAP];
+  __shared__ int w_i[NW][CAP];
   const int64_t row = blockIdx.x;
   const double* x = logits + row * row_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  CandList<TL> cl;
-  cl.init();
+  WarpCands<KC> wc{w_x[warp], w_i[warp], 0, -INFINITY, -1, false};
   double ref = -INFINITY, s = 0.0;
-  scan_row<VEC2>(x, V, [&](double v, int j) {
-    lse_add(ref, s, v);
-    if (cl.wants(v)) cl.insert(v, j);
-  });
-  double mx = cl.idx[0] >= 0 ? cl.x[0] : -INFINITY;   // this thread's max
-  const double my_last_x = cl.x[TL - 1];
-  const int my_last_i = cl.idx[TL - 1];
+  // Elements of one batch; every lane runs the same number of batches (elements past the row
+  // are -inf and invalid). The log-sum reference moves once per batch: when the batch max
+  // exceeds it by more than 256, so every exp argument is at most 256.
+  // (arrays of 8 with constant indices after unrolling; entries past nb are ignored)
+  auto batch = [&](const double (&v)[8], const int (&j)[8], const bool (&ok)[8], int nb) {
+    double mv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) mv[u] = (u < nb && ok[u]) ? v[u] : -INFINITY;
+    const double bm = fmax(fmax(fmax(mv[0], mv[1]), fmax(mv[2], mv[3])), fmax(fmax(mv[4], mv[5]), fmax(mv[6], mv[7])));
+    if (bm != -INFINITY && !(bm - ref <= 256.0)) {
+      s = (ref == -INFINITY) ? 0.0 : s * exp_fast(ref - bm);
+      ref = bm;
+    }
+    // an argument clamped at -708 (elements past the row are -inf) adds at most 2^-1022,
+    // nothing next to a sum that holds a term of 1
+    double e[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) e[u] = u < nb ? exp_fast(fmax(v[u] - ref, -708.0)) : 0.0;
+    s += ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));   // a tree: short dependency chain
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (u < nb) wc.offer(v[u], j[u], ok[u]);
+  };
+  if (VEC2) {
+    const double2* x2 = reinterpret_cast<const double2*>(x);
+    const int64_t n2 = V >> 1;
+    for (int64_t base = 0; base < n2; base += 4 * NT) {
+      double2 d[4];
+      bool okp[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t ii = base + u * NT + tid;
+        okp[u] = ii < n2;
+        d[u] = okp[u] ? __ldcs(x2 + ii) : make_double2(-INFINITY, -INFINITY);
+      }
+      double v[8];
+      int j[8];
+      bool ok[8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int jj = (int)(2 * (base + u * NT + tid));
+        v[2 * u] = d[u].x; v[2 * u + 1] = d[u].y;
+        j[2 * u] = jj; j[2 * u + 1] = jj + 1;
+        ok[2 * u] = okp[u]; ok[2 * u + 1] = okp[u];
+      }
+      batch(v, j, ok, 8);
+    }
+    if (V & 1) {   // the odd last element: lane 0 of warp 0, the warp calls together
+      if (warp == 0) {
+        double v[8] = {lane == 0 ? x[V - 1] : -INFINITY};
+        int j[8] = {(int)(V - 1)};
+        bool ok[8] = {lane == 0};
+        batch(v, j, ok, 1);
+      }
+    }
+  } else {
+    for (int64_t base = 0; base < V; base += 8 * NT) {
+      double v[8];
+      int j[8];
+      bool ok[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t ii = base + u * NT + tid;
+        ok[u] = ii < V;
+        v[u] = ok[u] ? x[ii] : -INFINITY;
+        j[u] = (int)ii;
+      }
+      batch(v, j, ok, 8);
+    }
+  }
+  wc.cut();   // the warp's KC best, in order
 
-  // (max, reference, sum): warp, then CTA
+  // (reference, sum): warp, then CTA
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
-    mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     const double orf = __shfl_xor_sync(0xffffffffu, ref, off);
     const double os = __shfl_xor_sync(0xffffffffu, s, off);
     const double nr = fmax(ref, orf);
@@ -235,17 +372,15 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
     }
     ref = nr;
   }
-  if (lane == 0) { s_m[warp] = mx; s_r[warp] = ref; s_s[warp] = s; }
-  merge_lists<KC, TL>(cl, s_cx, s_ci, s_fx, s_fi);
-
-  // a thread whose last candidate made the CTA's KC best may have dropped one more
-  const bool saturated =
-      my_last_i >= 0 && s_fi[KC - 1] >= 0 && !cand_before(s_fx[KC - 1], s_fi[KC - 1], my_last_x, my_last_i);
-  const int any_saturated = __syncthreads_or(saturated ? 1 : 0);
+  if (lane == 0) { s_r[warp] = ref; s_s[warp] = s; }
+  for (int c = lane; c < KC; c += 32) {
+    s_cx[warp * KC + c] = c < wc.n ? wc.x[c] : -INFINITY;
+    s_ci[warp * KC + c] = c < wc.n ? wc.i[c] : -1;
+  }
+  merge_warp_lists<KC>(s_cx, s_ci, s_fx, s_fi);
 
   if (tid == 0) {
-    double M = s_m[0];
-    for (int w = 1; w < NW; ++w) M = fmax(M, s_m[w]);
+    const double M = s_fi[0] >= 0 ? s_fx[0] : -INFINITY;   // the row max is the best candidate
     double S = 0.0;
     for (int w = 0; w < NW; ++w)
       if (s_r[w] != -INFINITY) S += s_s[w] * exp_fast(s_r[w] - M);
@@ -270,7 +405,7 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
       s_fi[c + 1] = iv;
     }
     const bool tie = V > KC && n == KC && s_flp[k - 1] == s_flp[KC - 1];
-    if (tie || any_saturated) {
+    if (tie) {
       top_idx[row * k] = -1;  // hands the row to block_topk_exact_kernel
     } else {
       for (int c = 0; c < k; ++c) {
