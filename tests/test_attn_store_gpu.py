@@ -103,3 +103,20 @@ def test_store_fp32_assembles_and_runs_the_regular_kernel(cuda):
     got = _run_store(c, cuda, torch.float32).cpu()
     ref, *_ = _oracle(c, torch.float32)
     assert (got - ref).abs().max().item() < 1e-4
+
+
+def test_store_with_ancestor_bits_as_the_hook_passes_them(cuda):
+    # the serving hook passes 64-bit ancestor words (cast_trees/serving.py:213-222), q as a strided view
+    c = _store_case(35, [300, 70, 1000], [40, 64, 9], poison=False)
+    bits = np.concatenate([otree.ancestor_words(c["parent"][int(a):int(b)]).reshape(-1)
+                           for a, b in zip(c["cu_q"][:-1], c["cu_q"][1:])]).astype(np.uint64).view(np.int64)
+    t = lambda a: torch.from_numpy(np.asarray(a)).to(cuda)
+    q_hm = c["q"].to(cuda, torch.bfloat16).transpose(0, 1).contiguous().transpose(0, 1)   # [T, H_q, D] view
+    out = cast_b200.varlen_tree_attention_store(q_hm, c["k_store"].to(cuda, torch.bfloat16),
+                                                c["v_store"].to(cuda, torch.bfloat16),
+                                                c["kp_hm"].to(cuda, torch.bfloat16).transpose(0, 1),
+                                                c["vp_hm"].to(cuda, torch.bfloat16).transpose(0, 1), t(c["cu_q"]),
+                                                t(c["S"]), t(c["P"]), t(bits))
+    assert _lib.device_error() == 0
+    ref, *_ = _oracle(c, torch.bfloat16)
+    assert (out.float().cpu() - ref).abs().max().item() < 2e-2
