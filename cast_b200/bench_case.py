@@ -147,6 +147,30 @@ def main():
         if _lib.device_error() != 0:
             raise RuntimeError("device error")
         rec["us_per_launch_graph"] = round(ev[0].elapsed_time(ev[1]) * 1e3 / args.iters, 1)
+    if args.what in ("attn", "attn_store"):
+        # achieved work against the measured peaks (MEASURED_PEAKS.json beside the package, else the
+        # earlier measurement on this pool); a kernel timed alone is compared with the burst figures
+        import pathlib
+        cnt = trees.count.cpu().tolist()
+        dep = trees.depth.cpu()
+        depth_sums = [int(dep[b, :cnt[b]].sum()) for b in range(w.B)]
+        flops, nbytes = w.attn_flops(depth_sums), w.attn_bytes()
+        t_s = rec["us_per_launch"] * 1e-6
+        peaks = pathlib.Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+        if peaks.exists():
+            pk = json.loads(peaks.read_text())
+            hbm, tf, src = float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
+        else:
+            hbm, tf, src = 6650.0, 1590.0, "fallback"
+        rec["tflops"] = round(flops / t_s / 1e12, 1)
+        rec["gbs"] = round(nbytes / t_s / 1e9, 1)
+        rec["hbm_floor_us"] = round(nbytes / (hbm * 1e9) * 1e6, 1)
+        if dtype != torch.float32:
+            rec["tensor_floor_us"] = round(flops / (tf * 1e12) * 1e6, 1)
+            bound = "tensor" if rec["tensor_floor_us"] >= rec["hbm_floor_us"] else "hbm"
+            rec["bound"] = bound
+            rec["frac_of_burst_peak"] = round((rec["tflops"] / tf) if bound == "tensor" else (rec["gbs"] / hbm), 3)
+        rec["peaks"] = src
     if args.what in ("walk", "append"):
         acc = walk_out.accepted.cpu()
         rec["mean_accepted"] = round(float(acc.float().mean()), 2)
