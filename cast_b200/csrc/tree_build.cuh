@@ -67,6 +67,30 @@ __device__ __forceinline__ double exp_fast(double t) {
   return p * __longlong_as_double((long long)(k + 1023) << 52);
 }
 
+// exp_fast for t >= -708 (callers clamp): no underflow check, 2^k is always a normal number.
+__device__ __forceinline__ double exp_fast_clamped(double t) {
+  constexpr double kLog2e = 1.4426950408889634;
+  constexpr double kLn2Hi = 0.6931471803691238;
+  constexpr double kLn2Lo = 1.9082149292705877e-10;
+  constexpr double kShift = 6755399441055744.0;
+  const double kd = fma(t, kLog2e, kShift);
+  const int k = __double2loint(kd);
+  const double kf = kd - kShift;
+  const double r = fma(-kf, kLn2Lo, fma(-kf, kLn2Hi, t));
+  double p = 2.755731922398589e-07;
+  p = fma(p, r, 2.7557319223985893e-06);
+  p = fma(p, r, 2.48015873015873e-05);
+  p = fma(p, r, 0.0001984126984126984);
+  p = fma(p, r, 0.001388888888888889);
+  p = fma(p, r, 0.008333333333333333);
+  p = fma(p, r, 0.041666666666666664);
+  p = fma(p, r, 0.16666666666666666);
+  p = fma(p, r, 0.5);
+  p = fma(p, r, 1.0);
+  p = fma(p, r, 1.0);
+  return p * __hiloint2double((k + 1023) << 20, 0);
+}
+
 // Folds one element into a thread's (reference, sum of exp(x - reference)).
 __device__ __forceinline__ void lse_add(double& ref, double& s, double v) {
   if (v == -INFINITY) return;
@@ -257,7 +281,8 @@ struct WarpCands {
   // One element per lane (valid = inside the row); every lane of the warp calls it.
   __device__ __forceinline__ void offer(double v, int j, bool valid) {
     const int lane = threadIdx.x & 31;
-    const bool pass = (v > tx && valid) || (valid && (!full || (v == tx && j < ti)));
+    // v >= tx admits a superset (equal values the cut then ranks by index): one comparison
+    const bool pass = valid && (!full || v >= tx);
     const unsigned mask = __ballot_sync(0xffffffffu, pass);
     if (mask) {
       if (pass) {
@@ -272,7 +297,7 @@ struct WarpCands {
 };
 
 template <int KC, bool VEC2>
-__global__ void __launch_bounds__(topk::NT)
+__global__ void __launch_bounds__(topk::NT, 4)   // four CTAs per SM: 64 registers
 block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
                   int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
   using namespace topk;
@@ -306,7 +331,7 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
     // nothing next to a sum that holds a term of 1
     double e[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) e[u] = u < nb ? exp_fast(fmax(v[u] - ref, -708.0)) : 0.0;
+    for (int u = 0; u < 8; ++u) e[u] = u < nb ? exp_fast_clamped(fmax(v[u] - ref, -708.0)) : 0.0;
     s += ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));   // a tree: short dependency chain
 #pragma unroll
     for (int u = 0; u < 8; ++u)
