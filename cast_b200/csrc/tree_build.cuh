@@ -29,7 +29,7 @@ namespace cast {
 // exact path: a second read that selects the top k on lp itself.
 // ---------------------------------------------------------------------------
 namespace topk {
-constexpr int NT = 256;
+constexpr int NT = 128;
 constexpr int NW = NT / 32;
 constexpr int TL = 8;  // candidates per thread in the common path
 }
@@ -297,7 +297,7 @@ struct WarpCands {
 };
 
 template <int KC, bool VEC2>
-__global__ void __launch_bounds__(topk::NT, 4)   // four CTAs per SM: 64 registers
+__global__ void __launch_bounds__(topk::NT, 8)   // eight CTAs per SM (64 registers): one wave of rows
 block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
                   int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
   using namespace topk;
