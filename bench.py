@@ -5,24 +5,43 @@ the drafter's fp64 block scores and GPU best-first tree build (pack parents
 written in the same launch) once per round, then one ragged tree-attention
 call per decoder layer consuming those parents (cast_trees/serving.py calls
 its attention hook once per layer of the target forward). Workload at N=1:
-BASELINE configuration 3 (B=64, N=127, prefix ~ U[4096,8192], Llama-3.1-8B
-attention geometry 32/8 heads, d=128, 32 layers, bf16, V=128256), synthetic;
-the layers share one synthetic K/V set (1.59 GB, far larger than L2, so each
-call streams it from HBM).
-With --gpus N (one process per GPU under torchrun) every rank runs its own
-64 sequences of the same recipe (weak scaling, no collective on the path).
+configuration 3 of cast_b200.workloads (B=64, N=127, prefix ~ U[4096,8192],
+Llama-3.1-8B attention geometry 32/8 heads, d=128, 32 layers, bf16,
+V=128256), synthetic; the layers share one synthetic K/V set (1.59 GB, far
+larger than L2, so each call streams it from HBM).
+
+With --gpus N (one process per GPU under torchrun) the job draws one batch of
+64 * N sequences of the same recipe (the first 64 are configuration 3) and
+splits it into equal-count shards of near-equal cost, 64 sequences per rank
+(weak scaling, no collective on the path); times are the max over ranks.
 
 Prints one JSON line (rank 0). `value` is attention TFLOP/s of the whole job
 (visible (query, key) pairs only, 4 flops per pair and dim) over the device
 time of the full step; `e2e` is the same metric through the public Python API
 with pinned host inputs copied in and the output copied out inside the timed
-region. `--impl reference` times the reference's CPU path (the oracle port of
-cast_trees' numpy block_topk/build_tree and the fp32 masked-softmax reference
-of tests/test_tree_attn.py) on the host cores.
+region. Beside the metric, measured outside the timed regions:
+  roofline   the attention kernel against the measured burst bf16 peak (the
+             kernel runs at full clocks inside the round); DRAM traffic per
+             launch only when --traffic-csv names an ncu capture of it
+  parity     max abs error of the timed attention output against the CPU
+             oracle on a seeded sample of sequences
+  config5    configuration 5: one fixed batch of 512 sequences sharded by cost
+             over the N GPUs (strong scaling), one attention call per tree
+             width N in {16..256}: l(N) (max over ranks), fraction of the
+             binding roofline, and the least-squares c0/c1 over 16 <= n <= 128
+             fed to cast_trees.width.predict_width when the reference package
+             is installed beside the repo (baseline/_ref)
+  cpu_baseline  (N=1) the oracle port of the reference's CPU path timed on a
+             sample of the same round on the host cores
+`--impl reference` times that CPU path (the reference's numpy tree builder and
+its fp32 masked-softmax attention, restated in oracle/) one sampled sequence
+per step, full round per step, and prints the same line with impl=reference.
+The CPU legs (cpu_baseline, parity, the reference arm) are the only users of
+oracle/, always outside the timed regions.
 """
 import argparse
+import csv
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -40,6 +59,9 @@ sys.path.insert(0, str(ROOT))
 METRIC = "tree-attn µs/call and TFLOP/s, B=64 N=127 ctx 4-8K; % of roofline at 1-8 GPUs"
 B_PER_RANK = 64
 N_NODES = 127
+LAYERS_DEFAULT = 32
+TOL_BF16 = 2e-2
+WIDTHS = (16, 24, 32, 48, 64, 96, 128, 256)
 
 
 def _env():
@@ -54,17 +76,33 @@ def _peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def _profile_traffic(name):
-    """dram bytes per launch from a committed ncu summary line 'traffic_bytes_per_launch[<name>]: X'."""
-    for f in sorted((ROOT / "profiles").glob("*.md")):
-        for line in f.read_text().splitlines():
-            key = f"traffic_bytes_per_launch[{name}]:"
-            if line.strip().startswith(key):
-                try:
-                    return float(line.split(":", 1)[1].strip().split()[0])
-                except ValueError:
-                    return None
-    return None
+def _traffic_from_csv(path, kernel="attn_tc_kernel"):
+    """dram read + write bytes per launch of `kernel` from an ncu --csv capture (raw or details page)."""
+    vals = {}
+    with open(path, newline="") as f:
+        rows = [r for r in csv.reader(f) if r]
+    head = next((i for i, r in enumerate(rows) if "Kernel Name" in r), None)
+    if head is None:
+        return None
+    cols = rows[head]
+    kn = cols.index("Kernel Name")
+    if "Metric Name" in cols:   # details page: one row per metric
+        mn, mv, mu = cols.index("Metric Name"), cols.index("Metric Value"), cols.index("Metric Unit")
+        scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+        for r in rows[head + 1:]:
+            if kernel in r[kn] and r[mn] in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+                vals.setdefault(r[mn], []).append(float(r[mv].replace(",", "")) * scale.get(r[mu], 1))
+    else:                       # raw page: one row per launch, one column per metric (units in the next row)
+        units = rows[head + 1]
+        for name in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            if name in cols:
+                c = cols.index(name)
+                sc = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}.get(units[c], 1)
+                vals[name] = [float(r[c].replace(",", "")) * sc for r in rows[head + 2:] if kernel in r[kn]]
+    if len(vals) != 2 or not all(vals.values()):
+        return None
+    n = min(len(v) for v in vals.values())
+    return sum(sum(v[:n]) for v in vals.values()) / n
 
 
 class ClockSampler:
@@ -120,10 +158,29 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def rank_workload(rank):
+def job_workload(world):
+    """The whole job's batch: 64 * world sequences of the configuration-3 recipe (seed 2)."""
     from cast_b200 import workloads
-    full = workloads.Workload("config3", 2, 128256, *workloads._ragged(2, B_PER_RANK * (rank + 1), 4096, 8192, (N_NODES,)))
-    return full.shard(list(range(rank * B_PER_RANK, (rank + 1) * B_PER_RANK)))
+    S, N = workloads._ragged(2, B_PER_RANK * world, 4096, 8192, (N_NODES,))
+    return workloads.Workload("config3", 2, 128256, S, N)
+
+
+def rank_workload(rank, world):
+    """This rank's 64 sequences: equal-count shards of near-equal attention cost."""
+    from cast_b200 import sharding
+    full = job_workload(world)
+    costs = [sharding.sequence_cost(s, p) for s, p in zip(full.S, full.P)]
+    return full.shard(sharding.equal_count_shards(costs, world, B_PER_RANK)[rank])
+
+
+def bench_config(args, world):
+    """The `config` object of the JSON line (identical for both arms)."""
+    return {"workload": f"config3: B=64/GPU, N=127 (P=128), prefix U[4096,8192], 32/8 heads, d=128, V=128256; "
+                        f"step = one verify round: block_topk + build_tree + {args.layers} tree-attention calls "
+                        f"(one per layer)",
+            "layers": args.layers, "global_batch": B_PER_RANK * world, "seq_len": "4096-8192 (ragged)",
+            "parallelism": f"sequence-sharded x{world} (equal-count cost-balanced shards), no collective",
+            "l2": "inputs larger than L2 (logits 0.98 GB + K/V 1.59 GB streamed per step)"}
 
 
 class Step:
@@ -167,18 +224,30 @@ class Step:
         return trees
 
 
-def run_cast(args):
+def _dist():
     import torch.distributed as dist
+    return dist
+
+
+def _max_over_ranks(vals, dev, world, op="max"):
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    if world > 1:
+        dist = _dist()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return t.tolist()
+
+
+def run_cast(args):
     rank, world, local = _env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        _dist().init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     import cast_b200
     from cast_b200 import _lib
 
-    w = rank_workload(rank)
+    w = rank_workload(rank, world)
     st = Step(w, dev)
     # host inputs (pinned): the e2e leg copies them every step
     h_logits = torch.empty((w.B, 15, w.V), dtype=torch.float64).pin_memory()
@@ -188,14 +257,14 @@ def run_cast(args):
     h_q, h_k, h_v = (x.cpu().pin_memory() for x in (st.q, st.k, st.v))
     st.out = torch.empty_like(st.q)
     h_out = torch.empty(st.out.shape, dtype=st.out.dtype).pin_memory()
-    ws = cast_b200.workspace_size(w.dtype, w.B, w.layout()["total_q"], w.H_q, w.H_kv, w.D,
-                                  w.layout()["max_pack"], w.layout()["max_kv"])
+    lay = w.layout()
+    ws = cast_b200.workspace_size(w.dtype, w.B, lay["total_q"], w.H_q, w.H_kv, w.D, lay["max_pack"], lay["max_kv"])
     st.ws = torch.empty(max(ws, 1), dtype=torch.uint8, device=dev)
 
-    # launches per step: block_topk + build_tree + attention (+ combine when the keys are split)
-    kernel, n_split, attn_launches = cast_b200.attention_plan(st.q, st.k, st.v, st.out, w.B, w.layout()["max_pack"],
-                                                              w.layout()["max_kv"])
-    launches_per_step = 3 + attn_launches * args.layers   # topk (fast + exact kernels), tree, attention
+    # launches per step: block_topk (fast + exact kernels) + build_tree + attention (+ combine when split)
+    kernel, n_split, attn_launches = cast_b200.attention_plan(st.q, st.k, st.v, st.out, w.B, lay["max_pack"],
+                                                              lay["max_kv"])
+    launches_per_step = 3 + attn_launches * args.layers
 
     for _ in range(args.warmup):
         trees = st.run(args.layers)
@@ -214,7 +283,7 @@ def run_cast(args):
     clk = ClockSampler(local).__enter__()      # sampled over both timed regions below
     time.sleep(0.3)                            # nvidia-smi start-up
     if world > 1:
-        dist.barrier()
+        _dist().barrier()
     torch.cuda.synchronize()
     t0.record(stream)
     for i in range(args.steps):
@@ -222,7 +291,7 @@ def run_cast(args):
     t1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
-        dist.barrier()
+        _dist().barrier()
     step_ms = t0.elapsed_time(t1) / args.steps
     attn_ms = statistics.mean(a.elapsed_time(b) for a, b in evs) / args.layers   # per call
     tree_ms = step_ms - attn_ms * args.layers
@@ -273,7 +342,7 @@ def run_cast(args):
     e2e_steps(max(1, args.warmup))
     torch.cuda.synchronize()
     if world > 1:
-        dist.barrier()
+        _dist().barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     e2e_steps(args.steps)
@@ -281,40 +350,40 @@ def run_cast(args):
     torch.cuda.synchronize()
     clk.__exit__(None, None, None)
     if world > 1:
-        dist.barrier()
+        _dist().barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    if _lib.device_error() != 0:
+        raise RuntimeError("device error in the timed regions")
 
     # max over ranks of every time; sums of work
-    t = torch.tensor([step_ms, attn_ms, tree_ms, e2e_ms], dtype=torch.float64, device=dev)
-    work = torch.tensor([flops, call_bytes], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(work, op=dist.ReduceOp.SUM)
-    step_ms, attn_ms, tree_ms, e2e_ms = t.tolist()
-    tot_flops, tot_bytes = work.tolist()
+    step_ms, attn_ms, tree_ms, e2e_ms = _max_over_ranks([step_ms, attn_ms, tree_ms, e2e_ms], dev, world)
+    tot_flops, tot_bytes = _max_over_ranks([flops, call_bytes], dev, world, op="sum")
     hbm, tf_burst, tf_sus, peak_kind = _peaks()
 
     value = tot_flops / (step_ms * 1e-3) / 1e12
     attn_tflops = call_flops / (attn_ms * 1e-3) / 1e12     # per GPU, dominant kernel, per call
     attn_gbs = call_bytes / (attn_ms * 1e-3) / 1e9
     topk_gbs = w.topk_bytes() / (tree_ms * 1e-3) / 1e9
-    # binding roofline of the attention kernel: the slower of the HBM and tensor floors. The
-    # kernel runs `layers` times back to back inside a long step (power-capped clocks), so the
-    # tensor peak is the sustained figure; the burst figure is reported beside it.
-    tf_peak = tf_sus
+    # binding roofline of the attention kernel: the slower of the HBM and tensor floors, against
+    # the burst peaks (the kernel's clocks stay near the maximum inside the round: see `clocks`)
     t_hbm = call_bytes / (hbm * 1e9)
-    t_tensor = call_flops / (tf_peak * 1e12)
+    t_tensor = call_flops / (tf_burst * 1e12)
     bound = "tensor" if t_tensor >= t_hbm else "hbm"
     if bound == "tensor":
-        roof = {"bound": "tensor", "achieved": round(attn_tflops, 2), "peak": tf_peak, "unit": "TFLOP/s",
-                "frac": round(attn_tflops / tf_peak, 4)}
+        roof = {"bound": "tensor", "achieved": round(attn_tflops, 2), "peak": tf_burst, "unit": "TFLOP/s",
+                "frac": round(attn_tflops / tf_burst, 4)}
     else:
         roof = {"bound": "hbm", "achieved": round(attn_gbs, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(attn_gbs / hbm, 4)}
-    roof["traffic"] = _profile_traffic("attn_config3")
-    roof["peak_source"] = (f"{peak_kind}: MEASURED_PEAKS.json bf16_tflops_sustained (kernel timed inside a long "
-                           f"step); hbm_gbs for the HBM floor")
-    roof["frac_of_burst_peak"] = round(attn_tflops / tf_burst, 4)
+    roof["traffic"] = _traffic_from_csv(args.traffic_csv) if args.traffic_csv else None
+    if roof["traffic"] is not None:
+        roof["traffic_over_algorithmic"] = round(roof["traffic"] / call_bytes, 3)
+        roof["traffic_source"] = f"ncu capture {args.traffic_csv}"
+    roof["peak_source"] = (f"{peak_kind}: MEASURED_PEAKS.json bf16_tflops (burst) for the tensor floor, hbm_gbs "
+                           f"for the HBM floor; achieved = algorithmic flops per call / CUDA-event time per call")
+    roof["frac_of_sustained_peak"] = round(attn_tflops / tf_sus, 4)
+    roof["algorithmic_flops_per_call"] = call_flops
+    roof["algorithmic_bytes_per_call"] = call_bytes
     roof["hbm_floor_us"] = round(t_hbm * 1e6, 1)
     roof["tensor_floor_us"] = round(t_tensor * 1e6, 1)
 
@@ -323,12 +392,7 @@ def run_cast(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded normal(scale=5) block scores 15x128256 fp64, q/k/v N(0,1)*0.5 bf16",
-        "config": {"workload": f"config3: B=64/GPU, N=127 (P=128), prefix U[4096,8192], 32/8 heads, d=128, "
-                               f"V=128256; step = one verify round: block_topk + build_tree + {args.layers} "
-                               f"tree-attention calls (one per layer)", "layers": args.layers,
-                   "global_batch": B_PER_RANK * world, "seq_len": "4096-8192 (ragged)",
-                   "parallelism": f"sequence-sharded x{world}, no collective",
-                   "l2": "inputs larger than L2 (logits 0.98 GB + K/V 1.59 GB streamed per step)"},
+        "config": bench_config(args, world),
         "attn_kernel": kernel, "attn_key_splits": n_split,
         "us_per_call": round(attn_ms * 1e3, 1),
         "attn_tflops_per_gpu": round(attn_tflops, 2),
@@ -344,11 +408,17 @@ def run_cast(args):
         "clocks": clk.summary(),
     }
     result["verify_round_rows"] = round_rows(st, trees, w, dev)
+    # CPU legs (oracle), outside every timed region
+    cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(w, trees, args)
+        cpu = cpu_baseline(w, st, trees, args)
+        result["cpu_baseline"] = cpu["baseline"]
+    result["parity"] = parity_check(w, st, trees, dev, world, rank, cpu)
+    if not args.no_config5:
+        result["config5"] = config5_sweep(dev, world, rank, hbm, tf_burst, args)
     if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        _dist().barrier()
+        _dist().destroy_process_group()
     if rank == 0:
         emit(result)
 
@@ -412,8 +482,7 @@ def round_rows(st, trees, w, dev, iters=10):
         res["mean_accepted"] = round(float(acc.mean()), 2)
         res["rows_walked"] = int(acc.sum())
         res["note"] = (f"{w.B} requests, V={V} bf16 target logits, select keeps 48 of {trees.token.shape[1]} "
-                       f"nodes per request, append covers {n_layers} layers x K,V; eager calls (host time "
-                       f"included), device-only times in profiles/")
+                       f"nodes per request, append covers {n_layers} layers x K,V; eager calls, host time included")
         from cast_b200 import _lib
         if _lib.device_error() != 0:
             res["error"] = "device error"
@@ -422,86 +491,239 @@ def round_rows(st, trees, w, dev, iters=10):
         return {"error": f"{type(e).__name__}: {e}"}
 
 
-def _cpu_sample(w, ids):
-    """Times the oracle (the reference's CPU algorithms) on sequences `ids` of w.
+def _seq_inputs(w, st, b):
+    """CPU copies of sequence b's q, k, v rows (the bench's own device inputs)."""
+    lay = w.layout()
+    cq, ckv = lay["cu_q"], lay["cu_kv"]
+    return (st.q[cq[b]:cq[b + 1]].cpu(), st.k[ckv[b]:ckv[b + 1]].cpu(), st.v[ckv[b]:ckv[b + 1]].cpu())
 
-    Returns (tree_seconds, attention_seconds_per_call, flops_per_call, trees):
-    numpy block_topk + heap build_tree once, then one fp32 masked-softmax
-    attention call (torch, all threads). q/k/v are drawn on the CPU.
+
+def _cpu_round(w, b, layers, qkv):
+    """The reference's CPU path for one sequence of the round, timed (oracle port).
+
+    numpy block_topk + heap build_tree (cast_trees/tree.py:20-49, single-threaded as in the
+    reference), then `layers` fp32 masked-softmax attention calls (tests/test_tree_attn.py:40-59,
+    torch with all threads). Returns (tree_s, attn_s, flops, tree, out).
     """
     from oracle import attn as oattn
     from oracle import tree as otree
-    sub = w.shard(ids)
-    lay = sub.layout()
-    g = torch.Generator().manual_seed(1234)
-    q = (torch.randn(lay["total_q"], w.H_q, w.D, generator=g) * 0.5).to(w.dtype)
-    k = (torch.randn(lay["total_kv"], w.H_kv, w.D, generator=g) * 0.5).to(w.dtype)
-    v = (torch.randn(lay["total_kv"], w.H_kv, w.D, generator=g) * 0.5).to(w.dtype)
-    logits = [sub.logits(b) for b in range(sub.B)]
+    logits = w.logits(b)
     t0 = time.perf_counter()
-    trees, words = [], []
-    for b in range(sub.B):
-        idx, lp = otree.block_topk(logits[b])
-        tr = otree.build_tree(idx, lp, sub.N[b])
-        trees.append(tr)
-        words.append(otree.ancestor_words(otree.pack_parent(tr.parent)))
+    idx, lp = otree.block_topk(logits)
+    tr = otree.build_tree(idx, lp, w.N[b])
+    words = [otree.ancestor_words(otree.pack_parent(tr.parent))]
     t1 = time.perf_counter()
-    oattn.tree_attention(q.float(), k.float(), v.float(), lay["cu_q"], lay["cu_kv"], lay["prefix_len"],
-                         lay["pack_len"], words)
+    q, k, v = (x.float() for x in qkv)
+    S, P = w.S[b], w.P[b]
+    out = None
+    for _ in range(layers):
+        out = oattn.tree_attention(q, k, v, [0, P], [0, S + P], [S], [P], words)
     t2 = time.perf_counter()
-    flops = sub.attn_flops([int(t.depth.sum()) for t in trees])
-    return t1 - t0, t2 - t1, flops, trees
+    flops = layers * 4 * w.H_q * w.D * (P * S + P + int(tr.depth.sum()))
+    return t1 - t0, t2 - t1, flops, tr, out
 
 
-def cpu_baseline(w, trees_gpu, args):
-    n = max(1, args.cpu_seqs)
+def cpu_baseline(w, st, trees_gpu, args):
+    """Oracle port of the reference's CPU path on a sample of this round (rank 0, N=1)."""
     torch.set_num_threads(os.cpu_count() or 1)
-    t_tree, t_attn, flops, trees = _cpu_sample(w, list(range(n)))
-    round_s = t_tree + args.layers * t_attn
+    ids = list(range(max(1, args.cpu_seqs)))
+    t_tree = t_attn = 0.0
+    flops = 0
     exact = True
-    for b in range(n):
+    outs = {}
+    for b in ids:
+        tt, ta, fl, tr, out = _cpu_round(w, b, args.layers, _seq_inputs(w, st, b))
+        t_tree += tt
+        t_attn += ta
+        flops += fl
+        outs[b] = out
         c = int(trees_gpu.count[b])
-        exact &= c == len(trees[b])
-        exact &= np.array_equal(trees_gpu.parent[b, :c].cpu().numpy(), trees[b].parent)
-        exact &= np.array_equal(trees_gpu.token[b, :c].cpu().numpy(), trees[b].token)
-        exact &= np.array_equal(trees_gpu.depth[b, :c].cpu().numpy(), trees[b].depth)
-    return {"value": round(args.layers * flops / round_s / 1e12, 6), "unit": "TFLOP/s",
+        exact &= c == len(tr)
+        exact &= np.array_equal(trees_gpu.parent[b, :c].cpu().numpy(), tr.parent)
+        exact &= np.array_equal(trees_gpu.token[b, :c].cpu().numpy(), tr.token)
+        exact &= np.array_equal(trees_gpu.depth[b, :c].cpu().numpy(), tr.depth)
+    base = {"value": round(flops / (t_tree + t_attn) / 1e12, 6), "unit": "TFLOP/s",
             "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{n} of the {w.B} config-3 sequences: numpy block_topk + heap build_tree once "
-                      f"({t_tree:.2f} s, 1 thread) and one fp32 masked-softmax attention call "
-                      f"({t_attn:.3f} s, torch, all threads) counted {args.layers}x (one per layer)",
+            "sample": f"{len(ids)} of the {w.B} sequences of this round, each a full round: numpy block_topk + "
+                      f"heap build_tree ({t_tree:.2f} s in all, 1 thread) and {args.layers} fp32 masked-softmax "
+                      f"attention calls ({t_attn:.2f} s in all, torch, all threads); measured, not projected",
             "tree_arrays_bit_exact_vs_gpu": bool(exact)}
+    return {"baseline": base, "outs": outs}
+
+
+def parity_check(w, st, trees, dev, world, rank, cpu=None):
+    """Max abs error of the timed attention output against the oracle on sampled sequences.
+
+    The output checked is the last timed call's (every layer reads the same inputs); the oracle
+    runs on the same bf16 inputs and on the GPU-built tree. Max over ranks.
+    """
+    from oracle import attn as oattn
+    from oracle import tree as otree
+    lay = w.layout()
+    cq = lay["cu_q"]
+    if cpu is not None:
+        outs = cpu["outs"]
+    else:
+        outs = {}
+        pp = trees.pack_parent.cpu().numpy()
+        ids = np.random.default_rng(1000 + rank).choice(w.B, size=2, replace=False).tolist()
+        for b in ids:
+            q, k, v = (x.float() for x in _seq_inputs(w, st, b))
+            words = [otree.ancestor_words(pp[cq[b]:cq[b + 1]])]
+            S, P = w.S[b], w.P[b]
+            outs[b] = oattn.tree_attention(q, k, v, [0, P], [0, S + P], [S], [P], words)
+    errs = [(st.out[cq[b]:cq[b + 1]].float().cpu() - o).abs() for b, o in outs.items()]
+    mx = max(e.max().item() for e in errs)
+    mean = statistics.mean(e.mean().item() for e in errs)
+    mx, = _max_over_ranks([mx], dev, world)
+    n, = _max_over_ranks([float(len(outs))], dev, world, op="sum")
+    return {"max_abs_err": mx, "mean_abs_err": round(mean, 7), "seqs_checked": int(n), "tolerance": TOL_BF16,
+            "ok": bool(mx < TOL_BF16),
+            "against": "fp32 CPU oracle of the masked-softmax reference on the same bf16 inputs and GPU trees"}
+
+
+def config5_sweep(dev, world, rank, hbm, tf_burst, args):
+    """Configuration 5 over the job's GPUs: one attention call per width, l(N), c1 and N*.
+
+    One fixed batch of 512 sequences (prefix U[2048,16384], Qwen3-8B geometry, V=151936),
+    sharded by sequence cost over the ranks (LPT, no collective on the path). Per width the
+    trees are built on the GPU from block scores drawn on the device (normal, scale 5), then one
+    ragged attention call over the rank's shard is timed (CUDA events, mean of `iters` after
+    two warm-ups); l(N) is the max over ranks. c0/c1 are the least-squares line over
+    16 <= n = N+1 <= 128 (the fit of cast_trees/width.py:22-27); predict_width of the reference
+    package (baseline/_ref) turns the curve into the deployed width N*.
+    """
+    try:
+        import cast_b200
+        from cast_b200 import _lib, sharding, workloads
+        base = workloads.config(5)
+        costs = [sharding.sequence_cost(s, 129) for s in base.S]
+        mine = sharding.lpt_shards(costs, world)[rank]
+        sub = base.shard(mine)
+        g = torch.Generator(device=dev).manual_seed(base.seed * 7919 + 17)
+        logits = torch.empty((sub.B, 15, sub.V), dtype=torch.float64, device=dev)
+        logits.normal_(generator=g).mul_(5.0)
+        idx, lp = cast_b200.block_topk_device(logits, 8)
+        del logits
+        rows = []
+        iters = args.config5_iters
+        for N in WIDTHS:
+            ww = workloads.with_width(sub, N)
+            lay = ww.layout()
+            t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+            cu_q = t(lay["cu_q"])
+            trees = cast_b200.build_trees(idx, lp, N, 8, max_budget=N, cu_q=cu_q, total_q=lay["total_q"])
+            q, k, v = ww.make_qkv(dev)
+            out = torch.empty_like(q)
+            a = (q, k, v, cu_q, t(lay["cu_kv"]), t(lay["prefix_len"]), t(lay["pack_len"]), None)
+            kw = dict(parent=trees.pack_parent, max_pack=lay["max_pack"], max_kv=lay["max_kv"], out=out)
+            for _ in range(2):
+                cast_b200.varlen_tree_attention(*a, **kw)
+            torch.cuda.synchronize()
+            if world > 1:
+                _dist().barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                cast_b200.varlen_tree_attention(*a, **kw)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / iters
+            depth_sums = trees.depth.sum(dim=1, dtype=torch.int64).cpu().tolist()
+            fl, by = ww.attn_flops(depth_sums), ww.attn_bytes()
+            ms, = _max_over_ranks([ms], dev, world)
+            fl, by = _max_over_ranks([fl, by], dev, world, op="sum")
+            t_h, t_t = by / (world * hbm * 1e9), fl / (world * tf_burst * 1e12)
+            rows.append(dict(N=N, n=N + 1, ms=round(ms, 4), tflops=round(fl / (ms * 1e-3) / 1e12, 1),
+                             gbs=round(by / (ms * 1e-3) / 1e9, 1), bound="tensor" if t_t >= t_h else "hbm",
+                             frac=round(max(t_h, t_t) / (ms * 1e-3), 4)))
+            del q, k, v, out, trees, a, kw
+            torch.cuda.empty_cache()
+        if _lib.device_error() != 0:
+            return {"error": "device error in the configuration-5 sweep"}
+        n = np.array([r["n"] for r in rows], float)
+        ms = np.array([r["ms"] for r in rows], float)
+        sel = (n >= 16) & (n <= 128)
+        c1, c0 = np.polyfit(n[sel], ms[sel], 1)
+        res = {"workload": f"config5: fixed B=512, prefix U[2048,16384], 32/8 heads, d=128, V=151936, "
+                           f"LPT-sharded over {world} GPU(s) (strong scaling); one attention call per width",
+               "batch": base.B, "shard_imbalance": round(sharding.imbalance(base.S, [129] * base.B,
+                                                                           sharding.lpt_shards(costs, world)), 4),
+               "iters": iters, "widths": [r["N"] for r in rows], "n": n.tolist(),
+               "l_ms": [r["ms"] for r in rows], "tflops": [r["tflops"] for r in rows],
+               "gbs": [r["gbs"] for r in rows], "bound": [r["bound"] for r in rows],
+               "frac": [r["frac"] for r in rows], "frac_basis": "binding floor (HBM or burst bf16) / l(N)",
+               "c0_ms": round(float(c0), 5), "c1_ms_per_packed_token": round(float(c1), 6)}
+        res["predict_width"] = _predict_width(n.tolist(), ms.tolist())
+        return res
+    except Exception as e:
+        return {"error": f"{type(e).__name__}: {e}"}
+
+
+def _predict_width(n, ms):
+    """cast_trees.width.predict_width of the installed reference package (default mass curve, no drafter time)."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "cast_trees" / "width.py").exists():
+        return {"unavailable": "reference package not installed beside the repo (baseline/_ref)"}
+    sys.path.insert(0, str(ref))
+    try:
+        from cast_trees.width import predict_width
+        p = predict_width(n, ms)
+        return {"c0_ms": round(p.c0, 5), "c1_ms_per_packed_token": round(p.c1, 6), "n_stop": int(p.n_stop),
+                "n_star": int(p.n_star), "crossed": bool(p.crossed), "text": str(p)}
+    except Exception as e:
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    finally:
+        sys.path.remove(str(ref))
 
 
 def run_reference(args):
+    """The reference's CPU path (oracle port) on the host cores, one sampled sequence per step.
+
+    Each step is a full verify round for one sequence of the same batch the cast arm runs
+    (sequence step mod 64 of rank 0's shard): numpy tree build once, then `layers` attention
+    calls. ms_per_step is the measured wall time of those steps; value = the attention flops
+    they did / that time.
+    """
     rank, world, local = _env()
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    w = rank_workload(0)
-    n = max(1, args.ref_seqs)
+    w = rank_workload(0, world)
+    g = torch.Generator().manual_seed(1234)
     times, flops = [], 0
+    t_tree_all = t_attn_all = 0.0
     for i in range(args.warmup + args.steps):
-        ids = [(i * n + j) % w.B for j in range(n)]
-        t_tree, t_attn, fl, _ = _cpu_sample(w, ids)
+        b = i % w.B
+        S, P = w.S[b], w.P[b]
+        qkv = ((torch.randn(P, w.H_q, w.D, generator=g) * 0.5).to(w.dtype),
+               (torch.randn(S + P, w.H_kv, w.D, generator=g) * 0.5).to(w.dtype),
+               (torch.randn(S + P, w.H_kv, w.D, generator=g) * 0.5).to(w.dtype))
+        t0 = time.perf_counter()
+        tt, ta, fl, _, _ = _cpu_round(w, b, args.layers, qkv)
+        t1 = time.perf_counter()
         if i >= args.warmup:
-            times.append(t_tree + args.layers * t_attn)
-            flops += fl * args.layers
+            times.append(t1 - t0)
+            flops += fl
+            t_tree_all += tt
+            t_attn_all += ta
     tot = sum(times)
     value = flops / tot / 1e12
+    sample = (f"one sequence per step (sequence step mod {w.B} of the batch), a full round each: numpy "
+              f"block_topk + heap build_tree (1 thread, {t_tree_all:.2f} s over the timed steps) and "
+              f"{args.layers} fp32 masked-softmax attention calls (torch, all threads, {t_attn_all:.2f} s); "
+              f"ms_per_step is the measured wall time of one such step")
     emit({
         "metric": METRIC, "impl": "reference", "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * tot / args.steps, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 inputs, fp32 compute",
-        "data": "synthetic (config-3 recipe)",
-        "config": {"workload": f"config3 sample: {n} sequences per step, one verify round (block_topk + "
-                               f"build_tree once, attention counted once per layer, {args.layers} layers)",
-                   "global_batch": n, "seq_len": "4096-8192 (ragged)", "parallelism": "host CPU",
-                   "layers": args.layers},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * tot / max(1, args.steps), 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded normal(scale=5) block scores 15x128256 fp64, q/k/v N(0,1)*0.5 bf16",
+        "config": bench_config(args, world),
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": f"{n} config-3 sequences per step; the reference is Python: "
-                                                   f"its numpy tree builder and its fp32 masked-softmax attention"},
+                         "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's path is Python on the host (numpy tree builder, torch fp32 masked softmax); its "
+                "only GPU piece, a Triton kernel, takes packs of at most 64 tokens and cannot run P=128",
     })
 
 
@@ -525,16 +747,19 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["cast", "reference"], default="cast")
-    ap.add_argument("--layers", type=int, default=32, help="attention calls per verify round (decoder layers)")
-    ap.add_argument("--cpu-seqs", type=int, default=8, help="sequences in the cpu_baseline sample")
-    ap.add_argument("--ref-seqs", type=int, default=2, help="sequences per step of --impl reference")
+    ap.add_argument("--layers", type=int, default=LAYERS_DEFAULT, help="attention calls per verify round")
+    ap.add_argument("--cpu-seqs", type=int, default=2, help="sequences in the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config5", action="store_true")
+    ap.add_argument("--config5-iters", type=int, default=5)
+    ap.add_argument("--traffic-csv", default=None,
+                    help="ncu --csv capture of attn_tc_kernel with dram__bytes_read/write.sum for roofline.traffic")
     args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
     if args.impl == "reference":
+        args.warmup = max(args.warmup, 0)
         run_reference(args)
     else:
+        args.warmup = max(args.warmup, 3)
         run_cast(args)
 
 

@@ -30,7 +30,8 @@ CAST_DEV_BAD_LAYOUT, CAST_DEV_BAD_PARENT, CAST_DEV_TIMEOUT, CAST_DEV_TREE_OVERFL
 EXPORTS = ("cast_strerror", "cast_version", "cast_device_error", "cast_tree_attn_fwd",
            "cast_tree_attn_workspace_size", "cast_tree_attn_plan", "cast_block_topk", "cast_build_tree",
            "cast_tree_attn_fwd_noalloc", "cast_tree_attn_store_fwd", "cast_tree_attn_store_workspace_size",
-           "cast_tree_walk_greedy", "cast_select_global_topk", "cast_append_store", "cast_gather_cache")
+           "cast_tree_walk_greedy", "cast_select_global_topk", "cast_append_store", "cast_gather_cache",
+           "cast_test_set_wait_limit_ns")
 CAST_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 
@@ -124,6 +125,8 @@ def lib():
     L.cast_gather_cache.restype = c_int
     L.cast_gather_cache.argtypes = [c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_vp, c_vp, c_int,
                                     c_vp, c_int, c_vp]
+    L.cast_test_set_wait_limit_ns.restype = None
+    L.cast_test_set_wait_limit_ns.argtypes = [ctypes.c_uint64]
     _LIB = L
     return L
 

@@ -8,6 +8,10 @@
     python -m cast_b200.bench_case --what select --config 5 --batch 512 --iters 20
     python -m cast_b200.bench_case --what append --config 3 --batch 64 --iters 20
 
+    python -m cast_b200.bench_case --what vs_triton --config 1
+    python -m cast_b200.bench_case --what vs_triton --config 2
+    python -m cast_b200.bench_case --what vs_triton --config 5 --batch 512 --width 32
+
 Builds the first `batch` sequences of the configuration (trees from the GPU
 tree builder), launches the chosen kernel `iters` times on one GPU and prints
 the mean CUDA-event time per launch. `attn_store` runs the same attention with
@@ -18,19 +22,143 @@ tree for a few levels; `select` splits a shared budget of 8 nodes per request
 over trees built at width 48; `append` appends each walk's accepted rows to
 32 layers of per-request stores in place. Meant to be wrapped by ncu with a kernel
 filter (`-k regex:attn_tc|block_topk|build_tree`).
+
+`vs_triton` times this library's attention against the reference's own GPU
+kernel (cast_trees/tree_attn.py:116-139, the Triton `_tree_attn_fwd`, imported
+unmodified from the reference package installed beside the repo in
+baseline/_ref) on the same inputs. That kernel takes packs of at most 64
+tokens (one int64 ancestor word per row), so it runs configuration 1 (fp32 and
+bf16), the configuration-2 sequences with N <= 63, and configuration 5 at one
+width N <= 63 (`--width`). Both are timed through their public calls (the
+reference's reads cu_q back to the host every call) and the reference's kernel
+also alone, on a precomputed tile schedule.
 """
 import argparse
 import json
 
+import numpy as np
 import torch
 
 import cast_b200
 from cast_b200 import _lib, workloads
 
 
+def _ancestor_bits(pack_parent, cu_q, pack_len, max_depth):
+    """int64 [total_q] ancestor bitmask of every pack token (bit j = pack index j), pack index < 64.
+
+    Equivalent of the reference's host loop (cast_trees/serving.py:213-222): a token's word is its
+    own bit or'ed with its parent's word, built here by walking up at most `max_depth` levels.
+    """
+    dev = pack_parent.device
+    total_q = pack_parent.shape[0]
+    q0 = torch.repeat_interleave(cu_q[:-1].long(), pack_len.long(), output_size=total_q)
+    local = torch.arange(total_q, device=dev) - q0
+    bits = torch.bitwise_left_shift(torch.ones_like(local), local)
+    cur = pack_parent.long()
+    for _ in range(max_depth + 1):
+        live = cur >= 0
+        if not bool(live.any()):
+            break
+        bits = torch.where(live, bits | torch.bitwise_left_shift(torch.ones_like(cur), cur.clamp(min=0)), bits)
+        cur = torch.where(live, pack_parent.long()[(q0 + cur.clamp(min=0))], cur)
+    return bits
+
+
+def _event_us(fn, iters):
+    fn()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    for _ in range(iters):
+        fn()
+    ev[1].record()
+    torch.cuda.synchronize()
+    return ev[0].elapsed_time(ev[1]) * 1e3 / iters
+
+
+def vs_triton(args, dev):
+    """This library's tree attention against the reference's Triton kernel on the same inputs."""
+    import sys
+    from pathlib import Path
+    ref_dir = Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+    if not (ref_dir / "cast_trees" / "tree_attn.py").exists():
+        print(json.dumps({"what": "vs_triton", "unavailable": "reference package not installed in baseline/_ref"}))
+        return
+    sys.path.insert(0, str(ref_dir))
+    from cast_trees import tree_attn as ref_ta
+    dtypes = {"bf16": [torch.bfloat16], "fp16": [torch.float16], "fp32": [torch.float32]}[args.dtype]
+    if args.config == 1:
+        dtypes = [torch.float32, torch.bfloat16]
+    base = workloads.config(args.config)
+    if args.config == 5:
+        base = workloads.with_width(base.shard(list(range(min(args.batch, base.B)))), args.width)
+    elif args.config == 2:
+        base = base.shard([b for b in range(base.B) if base.N[b] <= 63])
+    w = base
+    assert max(w.P) <= 64, "the reference kernel takes packs of at most 64 tokens"
+    lay = w.layout()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    if args.config == 5:
+        g = torch.Generator(device=dev).manual_seed(w.seed * 7919 + 17)
+        logits = torch.empty((w.B, 15, w.V), dtype=torch.float64, device=dev).normal_(generator=g).mul_(5.0)
+    else:
+        logits = t(w.logits_batch())
+    idx, lp = cast_b200.block_topk_device(logits, 8)
+    del logits
+    cu_q, cu_kv, prefix, pack = t(lay["cu_q"]), t(lay["cu_kv"]), t(lay["prefix_len"]), t(lay["pack_len"])
+    budget = torch.tensor(w.N, dtype=torch.int32, device=dev)
+    trees = cast_b200.build_trees(idx, lp, budget, 8, max_budget=max(w.N), cu_q=cu_q, total_q=lay["total_q"])
+    bits = _ancestor_bits(trees.pack_parent, cu_q, pack, 15)
+    rows = []
+    for dtype in dtypes:
+        q, k, v = w.make_qkv(dev, dtype)
+        out = torch.empty_like(q)
+        ours = lambda: cast_b200.varlen_tree_attention(q, k, v, cu_q, cu_kv, prefix, pack, None,
+                                                       parent=trees.pack_parent, max_pack=lay["max_pack"],
+                                                       max_kv=lay["max_kv"], out=out)
+        theirs = lambda: ref_ta.varlen_tree_attention(q, k, v, cu_q, cu_kv, prefix, pack, bits)
+        o_ref = theirs()                  # first call autotunes the Triton kernel
+        torch.cuda.synchronize()
+        o_ours = ours().clone()
+        o_bits = cast_b200.varlen_tree_attention(q, k, v, cu_q, cu_kv, prefix, pack, bits,
+                                                 max_pack=lay["max_pack"], max_kv=lay["max_kv"])
+        if _lib.device_error() != 0:
+            raise RuntimeError("device error")
+        us_ours = _event_us(ours, args.iters)
+        us_ref = _event_us(theirs, args.iters)
+        req, row0, nrows = ref_ta._tile_schedule(cu_q.cpu(), dev)
+        sm_scale = 1.0 / (w.D ** 0.5)
+        out_k = torch.empty_like(q)
+
+        def ref_kernel():
+            ref_ta._tree_attn[(req.numel(), w.H_q)](
+                q, k, v, out_k, bits, req, row0, nrows, cu_kv, prefix, pack, sm_scale,
+                q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+                v.stride(0), v.stride(1), v.stride(2), out_k.stride(0), out_k.stride(1), out_k.stride(2),
+                H_q=w.H_q, GROUP=w.H_q // w.H_kv, D=w.D, BLOCK_M=ref_ta.BLOCK_M)
+        us_ref_k = _event_us(ref_kernel, args.iters)
+        depth_sums = trees.depth.sum(dim=1, dtype=torch.int64).cpu().tolist()
+        fl = w.attn_flops(depth_sums)
+        kernel, n_split, _ = cast_b200.attention_plan(q, k, v, out, w.B, lay["max_pack"], lay["max_kv"])
+        rows.append({"dtype": str(dtype).replace("torch.", ""), "kernel": kernel, "key_splits": n_split,
+                     "us_ours": round(us_ours, 1), "us_ref_api": round(us_ref, 1), "us_ref_kernel": round(us_ref_k, 1),
+                     "speedup_vs_ref_api": round(us_ref / us_ours, 2),
+                     "speedup_vs_ref_kernel": round(us_ref_k / us_ours, 2),
+                     "tflops_ours": round(fl / (us_ours * 1e-6) / 1e12, 2),
+                     "tflops_ref_kernel": round(fl / (us_ref_k * 1e-6) / 1e12, 2),
+                     "max_abs_diff_ours_vs_ref": (o_ours.float() - o_ref.float()).abs().max().item(),
+                     "bits_and_parent_identical": bool(torch.equal(o_ours, o_bits))})
+        del q, k, v, out, out_k
+    print(json.dumps({"what": "vs_triton", "config": args.config, "batch": w.B,
+                      "width": args.width if args.config == 5 else None,
+                      "P": sorted(set(w.P)), "S_range": [min(w.S), max(w.S)], "rows": rows}))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--what", choices=["attn", "attn_store", "topk", "tree", "walk", "select", "append"], default="attn")
+    ap.add_argument("--what", choices=["attn", "attn_store", "topk", "tree", "walk", "select", "append", "vs_triton"],
+                    default="attn")
+    ap.add_argument("--width", type=int, default=32, help="vs_triton on configuration 5: tree width N (<= 63)")
     ap.add_argument("--config", type=int, default=3)
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--iters", type=int, default=3)
@@ -39,6 +167,9 @@ def main():
                     help="also time the calls replayed from a CUDA graph (device time without host overhead)")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
+    if args.what == "vs_triton":
+        vs_triton(args, dev)
+        return
     dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[args.dtype]
     w = workloads.config(args.config, dtype)
     w = w.shard(list(range(min(args.batch, w.B))))

@@ -45,6 +45,9 @@ struct AttnParams {
   // key tiles are ceil(S_b/128) prefix tiles then ceil(P_b/128) pack tiles.
   int store_mode;
   int store_rows, store_batch;
+  // Limit of the tensor-core kernel's pipeline waits (ns). The waits that let
+  // in-flight copies and MMAs drain before a CTA exits keep the full limit.
+  uint64_t wait_ns;
 };
 
 // Key tiles of one sequence: the whole range for the regular layout, the

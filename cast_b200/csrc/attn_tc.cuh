@@ -53,6 +53,9 @@ constexpr float kRescaleLog2 = 8.0f;          // lazy O rescale threshold (facto
 // warpgroup 0 (TMA, MMA, two idle warps) gives back to 104, the two softmax
 // warpgroups take 200: 128 x 104 + 256 x 200 = 64512.
 constexpr int kRegsLow = 104, kRegsHigh = 200;
+// Largest batch whose sequences the CTAs rank by length (longest first); larger
+// batches run in sequence order. The keys take 4 bytes each of the K ring.
+constexpr int kMaxRankedSeqs = 1024;
 
 __host__ __device__ inline int anc_tokens(int G) { return QT * BM / G + 2; }
 __host__ __device__ inline size_t smem_bytes(int G, int W) {
@@ -108,7 +111,43 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   __shared__ float comb_m[BM], comb_l[BM];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int b = blockIdx.y / p.H_kv, h = blockIdx.y % p.H_kv;
+  // Work unit of this CTA, longest sequences first. CTAs start in launch order (linear block
+  // index), so the launch-order index L is decoded as (rank of the sequence, KV head, key chunk,
+  // row block), row blocks fastest (the blocks of one head share its K/V tiles through L2), and
+  // the sequence of that rank is found by ranking every sequence by S + P (descending, lower
+  // index first): the longest units start first and the last wave holds the shortest ones.
+  const int L = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int mblk = L % gridDim.x;
+  int rest = L / gridDim.x;
+  const int split = rest % gridDim.z;
+  rest /= gridDim.z;
+  const int h = rest % p.H_kv;
+  const int rank = rest / p.H_kv;
+  __shared__ int seq_of_rank;
+  {
+    int* keys = reinterpret_cast<int*>(smem + SMEM_K);   // scratch before any TMA load lands there
+    if (p.B <= kMaxRankedSeqs) {
+      for (int i = tid; i < p.B; i += NT) {
+        const long long k = (long long)p.prefix_len[i] + p.pack_len[i];
+        keys[i] = (int)max(-1LL, min(k, 0x7fffffffLL));
+      }
+      __syncthreads();
+      for (int i = tid; i < p.B; i += NT) {
+        const int ki = keys[i];
+        int r = 0;
+        for (int j = 0; j < p.B; ++j) {
+          const int kj = keys[j];
+          r += (kj > ki || (kj == ki && j < i)) ? 1 : 0;
+        }
+        if (r == rank) seq_of_rank = i;
+      }
+    } else if (tid == 0) {
+      seq_of_rank = rank;
+    }
+    fence_proxy_async_smem();   // the keys' generic-proxy writes are ordered before the TMA copies into this area
+    __syncthreads();
+  }
+  const int b = seq_of_rank;
   SeqMeta m;
   if constexpr (STORE) {
     m.q0 = p.cu_q[b]; m.kv0 = 0; m.S = p.prefix_len[b]; m.P = p.pack_len[b];
@@ -118,12 +157,12 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
     m = load_seq(p.cu_q, p.cu_kv, p.prefix_len, p.pack_len, b, p.total_q, p.total_kv, p.max_pack, p.max_kv);
   }
   if (!m.ok) {
-    if (tid == 0 && blockIdx.x == 0 && blockIdx.z == 0) report(CAST_DEV_BAD_LAYOUT);
+    if (tid == 0 && mblk == 0 && split == 0) report(CAST_DEV_BAD_LAYOUT);
     return;
   }
   const int G = p.G;
   const int rows = G * m.P;
-  const int r_base = blockIdx.x * (QT * BM);
+  const int r_base = mblk * (QT * BM);
   if (r_base >= rows) return;
   const int n_qt = (rows - r_base > BM) ? 2 : 1;
   const int nkeys = m.S + m.P;
@@ -135,13 +174,13 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
     nt_pre = (m.S + BN - 1) / BN;
     const int nt_all = nt_pre + (m.P + BN - 1) / BN;
     const int ct = p.chunk / BN;
-    t_begin = blockIdx.z * ct;
+    t_begin = split * ct;
     if (t_begin >= nt_all) return;
     n_kt = min(nt_all, t_begin + ct) - t_begin;
     k_begin = 0;
     k_end = nkeys;
   } else {
-    k_begin = blockIdx.z * p.chunk;
+    k_begin = split * p.chunk;
     if (k_begin >= nkeys) return;
     k_end = min(nkeys, k_begin + p.chunk);
     n_kt = (k_end - k_begin + BN - 1) / BN;
@@ -174,7 +213,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
     }
     for (int q = 0; q < QT; ++q) {
       mbar_init(smem_u32(&bars.s_full[q]), 1);
-      mbar_init(smem_u32(&bars.p_full[q]), BM);
+      mbar_init(smem_u32(&bars.p_full[q]), BM / 32);   // one arrival per softmax warp
     }
     mbar_init(smem_u32(&bars.o_full), 1);
     mbar_init(smem_u32(&bars.comb), BM);
@@ -209,7 +248,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       }
     }
     __syncwarp();
-    int issued = 0;
+    int issued_k = 0, issued_v = 0;   // K / V tiles whose copies were issued
     for (int j = 0; j < n_kt; ++j) {
       const int s = j % NST;
       const uint32_t use = (uint32_t)(j / NST);
@@ -226,31 +265,29 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
           }
         }
       };
-      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.k_empty[s]), (use - 1) & 1, abort_flag)))
+      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.k_empty[s]), (use - 1) & 1, abort_flag, p.wait_ns)))
         break;
       if (elect_one()) {
         mbar_expect_tx(smem_u32(&bars.k_full[s]), TILE_BYTES);
         load_tile(&tmK, &tmKp, smem_u32(smem + SMEM_K + s * TILE_BYTES), smem_u32(&bars.k_full[s]));
       }
       __syncwarp();
-      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.v_empty[s]), (use - 1) & 1, abort_flag))) {
-        issued = j + 1;  // K of tile j is in flight
+      issued_k = j + 1;
+      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.v_empty[s]), (use - 1) & 1, abort_flag, p.wait_ns)))
         break;
-      }
       if (elect_one()) {
         mbar_expect_tx(smem_u32(&bars.v_full[s]), TILE_BYTES);
         load_tile(&tmV, &tmVp, smem_u32(smem + SMEM_V + s * TILE_BYTES), smem_u32(&bars.v_full[s]));
       }
       __syncwarp();
-      issued = j + 1;
+      issued_v = j + 1;
     }
-    // let the last copies land before the CTA can exit (immediate on the normal path)
-    for (int j = max(0, issued - NST); j < issued; ++j) {
-      const int s = j % NST;
-      const uint32_t ph = (uint32_t)(j / NST) & 1;
-      mbar_wait(smem_u32(&bars.k_full[s]), ph, nullptr);
-      mbar_wait(smem_u32(&bars.v_full[s]), ph, nullptr);
-    }
+    // let the last copies land before the CTA can exit (immediate on the normal path); only
+    // copies that were issued are waited for
+    for (int j = max(0, issued_k - NST); j < issued_k; ++j)
+      mbar_wait(smem_u32(&bars.k_full[j % NST]), (uint32_t)(j / NST) & 1, nullptr);
+    for (int j = max(0, issued_v - NST); j < issued_v; ++j)
+      mbar_wait(smem_u32(&bars.v_full[j % NST]), (uint32_t)(j / NST) & 1, nullptr);
     mbar_wait(qf, 0, nullptr);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -291,7 +328,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       __syncwarp();
     };
     auto wait_all = [&](uint64_t& bar, uint32_t parity) {
-      return __all_sync(0xffffffffu, mbar_wait(smem_u32(&bar), parity, abort_flag));
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(&bar), parity, abort_flag, p.wait_ns));
     };
     // Store mode: the last prefix tile also holds store rows past the prefix; their scores
     // are masked, but 0 x (a non-finite stale value) would still poison P V, so those V rows
@@ -417,7 +454,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       // are made with per-lane values inside uniform branches).
       uint32_t sv[BN];
       for (int j = 0; j < n_steps; ++j) {
-        ok = mbar_wait(smem_u32(&bars.s_full[q]), (uint32_t)j & 1, abort_flag);
+        ok = mbar_wait(smem_u32(&bars.s_full[q]), (uint32_t)j & 1, abort_flag, p.wait_ns);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         fence_after_sync();
         int n0, klim;
@@ -498,10 +535,11 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
         }
         tmem_st_wait();
         fence_before_sync();
-        mbar_arrive(smem_u32(&bars.p_full[q]));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bars.p_full[q]));
       }
       // epilogue: O / l, or the unnormalised partial of this key chunk
-      bool done = mbar_wait(smem_u32(&bars.o_full), 0, ok ? abort_flag : nullptr);
+      bool done = ok ? mbar_wait(smem_u32(&bars.o_full), 0, abort_flag, p.wait_ns) : mbar_wait(smem_u32(&bars.o_full), 0, nullptr);
       done = __all_sync(0xffffffffu, done && ok);
       fence_after_sync();
       // dual mode: the odd-tile warpgroup hands its (m, l) over; the even one merges the two
@@ -514,7 +552,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
           mbar_arrive(smem_u32(&bars.comb));
           done = false;
         } else {
-          done = __all_sync(0xffffffffu, done && mbar_wait(smem_u32(&bars.comb), 0, abort_flag));
+          done = __all_sync(0xffffffffu, done && mbar_wait(smem_u32(&bars.comb), 0, abort_flag, p.wait_ns));
           if (done) {
             const float m1 = comb_m[t], l1 = comb_l[t];
             const float mx = fmaxf(m_ref, m1);
@@ -560,7 +598,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
             }
           }
         } else {
-          const int64_t slot = ((int64_t)blockIdx.z * p.total_q + tq) * p.H_q + hq;
+          const int64_t slot = ((int64_t)split * p.total_q + tq) * p.H_q + hq;
           float* O = p.ws_o + slot * D;
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {

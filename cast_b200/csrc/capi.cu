@@ -6,6 +6,7 @@
 #include <stdio.h>
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -19,6 +20,9 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 std::atomic<int> g_sm_count[kMaxDevices];
+// Limit of the tensor-core kernel's pipeline waits for the launches that follow
+// (cast_test_set_wait_limit_ns); the default is the library-wide wait limit.
+std::atomic<uint64_t> g_pipeline_wait_ns{tc::kWaitLimitNs};
 
 int sm_count() {
   int dev = 0;
@@ -233,19 +237,49 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[CAST_NOALLOC_SC
 
 namespace cast {
 namespace {
-std::atomic<void*> g_noalloc_ptr[kMaxDevices];
+// Per device: the context the cached address belongs to, and the address.
+struct NoallocSlot {
+  std::mutex mu;
+  CUcontext ctx = nullptr;
+  void* ptr = nullptr;
+};
+NoallocSlot g_noalloc[kMaxDevices];
+
+PFN_cuCtxGetCurrent_v4000 ctx_get_current() {
+  static std::atomic<void*> fn{nullptr};
+  void* f = fn.load(std::memory_order_acquire);
+  if (f) return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 4000, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || f == nullptr)
+    return nullptr;
+  fn.store(f, std::memory_order_release);
+  return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+}
 
 // Device address of g_noalloc_scratch on the current device (nullptr on failure).
+// The address is looked up once per context: a device reset (cudaDeviceReset)
+// destroys the context and the library's module with it, so a call after a reset
+// sees a new current context and looks the address up again in it.
 void* noalloc_scratch() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  void* ptr = g_noalloc_ptr[dev].load(std::memory_order_acquire);
-  if (ptr) return ptr;
+  auto get_ctx = ctx_get_current();
+  if (!get_ctx) return nullptr;
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return nullptr;
+  NoallocSlot& slot = g_noalloc[dev];
+  std::lock_guard<std::mutex> lock(slot.mu);
+  if (ctx != nullptr && slot.ptr != nullptr && slot.ctx == ctx) return slot.ptr;
+  // (no current context yet: the lookup below makes the device's primary context current)
+  void* ptr = nullptr;
   if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
     cudaGetLastError();
     return nullptr;
   }
-  g_noalloc_ptr[dev].store(ptr, std::memory_order_release);
+  if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return nullptr;
+  slot.ctx = ctx;
+  slot.ptr = ptr;
   return ptr;
 }
 }  // namespace
@@ -277,6 +311,10 @@ const char* cast_strerror(int status) {
 }
 
 int cast_version(void) { return 100; }
+
+void cast_test_set_wait_limit_ns(uint64_t ns) {
+  g_pipeline_wait_ns.store(ns == 0 ? tc::kWaitLimitNs : ns, std::memory_order_relaxed);
+}
 
 int cast_device_error(cast_stream_t stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -365,6 +403,7 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
   const float scale = sm_scale > 0.f ? sm_scale : 1.0f / sqrtf((float)D);
   p.scale_log2 = scale * kLog2e;
   p.max_pack = max_pack; p.max_kv = max_kv;
+  p.wait_ns = g_pipeline_wait_ns.load(std::memory_order_relaxed);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (tc_eligible(dtype, D, p.G, strides, q, k, v, out)) {
@@ -467,6 +506,7 @@ int cast_tree_attn_store_fwd(const void* q, const void* k_store, const void* v_s
   p.scale_log2 = scale * kLog2e;
   p.max_pack = max_pack; p.max_kv = max_prefix + max_pack;
   p.store_mode = 1; p.store_rows = store_rows; p.store_batch = store_batch;
+  p.wait_ns = g_pipeline_wait_ns.load(std::memory_order_relaxed);
 
   const TcPlan pl = plan_tc_store(B, total_q, H_q, H_kv, max_pack, max_prefix, sms);
   if (pl.ws_bytes > 0) {

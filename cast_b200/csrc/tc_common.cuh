@@ -51,8 +51,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 
 // Waits for the phase with the given parity. `abort` (shared memory) lets the
-// other roles of the CTA give up at once after one of them timed out.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+// other roles of the CTA give up at once after one of them timed out; `limit_ns`
+// bounds the wait (the default everywhere except a kernel's pipeline waits,
+// whose limit a test may shorten to make one run out).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
@@ -60,7 +63,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     if (mbar_try_wait(bar, parity)) return true;
     if ((++n & 63u) == 0) {
       if (abort != nullptr && *abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         if (abort != nullptr) *abort = 1;
         report(CAST_DEV_TIMEOUT);
         return false;

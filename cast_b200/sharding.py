@@ -27,6 +27,26 @@ def lpt_shards(costs, n_shards):
     return [sorted(x) for x in shards]
 
 
+def equal_count_shards(costs, n_shards, per_shard):
+    """LPT with a cardinality cap: exactly `per_shard` indices per shard.
+
+    For weak scaling the per-GPU batch size is fixed; the largest cost goes
+    first onto the least-loaded shard that still has room. Needs
+    len(costs) == n_shards * per_shard. Each list is sorted ascending.
+    """
+    if n_shards < 1 or per_shard < 0 or len(costs) != n_shards * per_shard:
+        raise ValueError("need n_shards >= 1 and len(costs) == n_shards * per_shard")
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    heap = [(0, s) for s in range(n_shards)]
+    shards = [[] for _ in range(n_shards)]
+    for i in order:
+        load, s = heapq.heappop(heap)
+        shards[s].append(i)
+        if len(shards[s]) < per_shard:
+            heapq.heappush(heap, (load + costs[i], s))
+    return [sorted(x) for x in shards]
+
+
 def shard_of(prefix_len, pack_len, rank, world):
     """Sequence indices this rank processes."""
     costs = [sequence_cost(s, p) for s, p in zip(prefix_len, pack_len)]

@@ -122,7 +122,7 @@ def _ragged(seed, B, s_lo, s_hi, widths):
 
 
 def config(n, dtype=None):
-    """BASELINE configuration n (1..5)."""
+    """Benchmark configuration n (1..5) of the recipe in this module's docstring."""
     if n == 1:
         return Workload("config1", 0, 64, [512], [16], dtype or torch.float32, qkv_scale=1.0, cfg1_recipe=True)
     if n == 2:

@@ -84,6 +84,20 @@ int cast_version(void);
 int cast_device_error(cast_stream_t stream);
 
 /*
+ * Testing hook (no counterpart in the reference). Sets, for every launch of
+ * the tensor-core attention kernel this process makes afterwards, the limit
+ * in nanoseconds of the kernel's pipeline waits (a TMA copy or MMA it waits
+ * for, a ring slot, a softmax hand-off); 0 restores the default (1 s). With a
+ * limit shorter than a copy takes, a wait runs out: the CTA records
+ * CAST_DEV_TIMEOUT (read with cast_device_error), lets its in-flight copies
+ * and MMAs finish under the full limit, frees its tensor memory and returns,
+ * so the failure path can be tested without a hang or a fault. Results of a
+ * call that timed out are undefined; later calls are unaffected once the
+ * default is restored.
+ */
+void cast_test_set_wait_limit_ns(uint64_t ns);
+
+/*
  * Ragged ancestor-masked GQA tree attention, forward.
  * Replaces cast_trees/tree_attn.py:116 varlen_tree_attention and the kernel
  * it launches (tree_attn.py:17-92).
@@ -138,7 +152,10 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
  *     CAST_ERR_SCRATCH_LIMIT before anything is launched.
  *   - The first call on each device looks up the scratch array's device
  *     address (cudaGetSymbolAddress) with that device current; make that first
- *     call before any stream capture begins.
+ *     call before any stream capture begins. The address is kept per context:
+ *     after cudaDeviceReset (which unloads the library's module with the
+ *     context) the next call sees the new context and looks the address up
+ *     again, so that call, too, belongs before any capture.
  *   - Every call on a device shares the one scratch array, which keeps the
  *     last call's contents. Calls whose kernels may overlap on the GPU (other
  *     streams, other host threads) race on it: issue them on one stream, or

@@ -10,7 +10,7 @@ GPU tests pin the CUDA library against them.
 
 Files written next to this script:
   tree_cfg1.npz     block_topk of rng(0).normal(scale=5, (15, 64)) and
-                    build_tree at N = 16 and N = 127 (BASELINE config 1 and the
+                    build_tree at N = 16 and N = 127 (configuration 1 and the
                     quickstart's expected accepted length)
   tree_cases.npz    build_tree on assorted (L, V, k, budget) cases, including
                     integer logits that force ties in both the sort and the heap

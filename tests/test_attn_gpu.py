@@ -1,7 +1,7 @@
 """Tree attention on the GPU (through the C ABI) against the CPU oracle.
 
 Tolerances (max abs error against the fp32 oracle on the same inputs):
-fp32 inputs 1e-4, bf16 / fp16 inputs 2e-2, the bounds BASELINE states; the
+fp32 inputs 1e-4, bf16 / fp16 inputs 2e-2, the path's stated bounds; the
 reference test's own bound (max 5e-2, mean 5e-3) is also checked for the
 reference scenario.
 """

@@ -54,3 +54,23 @@ def test_cache_layers_handles_both_layouts():
 
 def test_select_global_topk_of_no_trees_is_empty():
     assert cast_b200.select_global_topk([], 10) == []
+
+
+def test_ancestor_bits_match_the_oracle_words():
+    # the int64 word the reference's Triton kernel takes, built on the torch side for the head-to-head
+    import numpy as np
+    import torch
+    from cast_b200.bench_case import _ancestor_bits
+    from oracle import tree as otree
+    rng = np.random.default_rng(5)
+    parents, cu = [], [0]
+    for P in (1, 17, 64, 33):
+        par = [-1] + [int(rng.integers(max(0, i - 5), i)) for i in range(1, P)]
+        parents += par
+        cu.append(cu[-1] + P)
+    pp = torch.tensor(parents, dtype=torch.int32)
+    cu_q = torch.tensor(cu, dtype=torch.int32)
+    got = _ancestor_bits(pp, cu_q, cu_q[1:] - cu_q[:-1], 64).numpy()
+    want = np.concatenate([otree.ancestor_words(np.array(parents[cu[b]:cu[b + 1]], np.int32)).reshape(-1)
+                           for b in range(4)]).view(np.int64)
+    assert np.array_equal(got, want)

@@ -27,6 +27,21 @@ def test_lpt_small_cases():
         sharding.lpt_shards([1], 0)
 
 
+def test_equal_count_shards_balance_the_weak_scaling_batch():
+    # 64 sequences per GPU of the configuration-3 recipe, drawn as one batch of 64 * world
+    for world in (1, 2, 4, 8):
+        S, N = workloads._ragged(2, 64 * world, 4096, 8192, (127,))
+        costs = [sharding.sequence_cost(s, n + 1) for s, n in zip(S, N)]
+        shards = sharding.equal_count_shards(costs, world, 64)
+        assert all(len(sh) == 64 for sh in shards)
+        assert sorted(i for sh in shards for i in sh) == list(range(64 * world))
+        loads = [sum(costs[i] for i in sh) for sh in shards]
+        assert max(loads) / (sum(loads) / world) < 1.002
+    assert sharding.equal_count_shards([9, 1, 8, 2], 2, 2) == [[0, 1], [2, 3]]
+    with pytest.raises(ValueError):
+        sharding.equal_count_shards([1, 2, 3], 2, 2)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

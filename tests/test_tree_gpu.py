@@ -133,7 +133,7 @@ def test_pack_layout_matches_serving_convention(cuda):
 
 
 def test_config3_rows_bit_exact(cuda):
-    # BASELINE config 3 block scores (V = 128256): GPU tree arrays equal the reference's
+    # configuration-3 block scores (V = 128256): GPU tree arrays equal the reference's
     w = workloads.config(3)
     sub = w.shard([0, 1, 2])
     logits = torch.from_numpy(sub.logits_batch()).to(cuda)
