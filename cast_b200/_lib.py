@@ -20,7 +20,7 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", 
 
 # status codes of include/cast_b200.h
 CAST_OK = 0
-CAST_F32, CAST_BF16, CAST_F16 = 0, 1, 2
+CAST_F32, CAST_BF16, CAST_F16, CAST_F32_SPLIT = 0, 1, 2, 3
 CAST_MAX_PACK = 1024
 CAST_MAX_TOPK = 24
 CAST_MAX_DEPTH = 64
@@ -31,7 +31,7 @@ EXPORTS = ("cast_strerror", "cast_version", "cast_device_error", "cast_tree_attn
            "cast_tree_attn_workspace_size", "cast_tree_attn_plan", "cast_block_topk", "cast_build_tree",
            "cast_tree_attn_fwd_noalloc", "cast_tree_attn_store_fwd", "cast_tree_attn_store_workspace_size",
            "cast_tree_walk_greedy", "cast_select_global_topk", "cast_append_store", "cast_gather_cache",
-           "cast_test_set_wait_limit_ns")
+           "cast_test_set_wait_limit_ns", "cast_tree_attn_workspace_size_kv")
 CAST_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 
@@ -105,6 +105,8 @@ def lib():
     L.cast_tree_attn_plan.argtypes = [c_int] * 8 + [c_vp] * 6
     L.cast_tree_attn_workspace_size.restype = c_sz
     L.cast_tree_attn_workspace_size.argtypes = [c_int] * 8
+    L.cast_tree_attn_workspace_size_kv.restype = c_sz
+    L.cast_tree_attn_workspace_size_kv.argtypes = [c_int] * 9
     L.cast_block_topk.restype = c_int
     L.cast_block_topk.argtypes = [c_vp, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp]
     L.cast_build_tree.restype = c_int

@@ -10,7 +10,8 @@
 
     python -m cast_b200.bench_case --what vs_triton --config 1
     python -m cast_b200.bench_case --what vs_triton --config 2
-    python -m cast_b200.bench_case --what vs_triton --config 5 --batch 512 --width 32
+    python -m cast_b200.bench_case --what vs_triton --config 0
+    python -m cast_b200.bench_case --what vs_triton --config 5 --batch 64 --width 32
 
 Builds the first `batch` sequences of the configuration (trees from the GPU
 tree builder), launches the chosen kernel `iters` times on one GPU and prints
@@ -29,7 +30,9 @@ unmodified from the reference package installed beside the repo in
 baseline/_ref) on the same inputs. That kernel takes packs of at most 64
 tokens (one int64 ancestor word per row), so it runs configuration 1 (fp32 and
 bf16), the configuration-2 sequences with N <= 63, and configuration 5 at one
-width N <= 63 (`--width`). Both are timed through their public calls (the
+width N <= 63 (`--width`, on a batch small enough for the reference kernel's
+32-bit element offsets: 64 sequences); `--config 0` runs the reference test's
+own scenario. Both are timed through their public calls (the
 reference's reads cu_q back to the host every call) and the reference's kernel
 also alone, on a precomputed tile schedule.
 """
@@ -76,6 +79,58 @@ def _event_us(fn, iters):
     return ev[0].elapsed_time(ev[1]) * 1e3 / iters
 
 
+def _ref_offsets_unsafe(total_q, total_kv, H_q, H_kv, D):
+    """Why the reference kernel must not run on these sizes, or None.
+
+    Its element offsets (row * stride, cast_trees/tree_attn.py:44-58) are 32-bit; a tensor of 2^31
+    elements or more overflows them and the kernel reads out of bounds (on this pool it raised an
+    illegal memory access on configuration 5's 4.8e9-element K/V).
+    """
+    if max(total_q * H_q * D, total_kv * H_kv * D) >= 2 ** 31:
+        return ("q/k/v hold 2^31 elements or more: the reference kernel's 32-bit offsets overflow "
+                "(illegal memory access on this pool); use a smaller --batch")
+    return None
+
+
+def vs_triton_scenario(args, dev, ref_ta):
+    """The reference test's own scenario (cast_trees tests/test_tree_attn.py:11-37 shape: B=8, 32/8 heads,
+    D=128, S in [200, 400), P in [2, 64), uniform random parents, N(0,1) inputs) through both kernels."""
+    g = torch.Generator().manual_seed(0)
+    qs, ks, vs, bits, S, P, cu_q, cu_kv = [], [], [], [], [], [], [0], [0]
+    for _ in range(8):
+        s_b = int(torch.randint(200, 400, (1,), generator=g))
+        p_b = int(torch.randint(2, 64, (1,), generator=g))
+        parent = [-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, p_b)]
+        qs.append(torch.randn(p_b, 32, 128, generator=g))
+        ks.append(torch.randn(s_b + p_b, 8, 128, generator=g))
+        vs.append(torch.randn(s_b + p_b, 8, 128, generator=g))
+        for i in range(p_b):
+            wd, j = 0, i
+            while j != -1:
+                wd |= 1 << j
+                j = parent[j]
+            bits.append(wd)
+        S.append(s_b)
+        P.append(p_b)
+        cu_q.append(cu_q[-1] + p_b)
+        cu_kv.append(cu_kv[-1] + s_b + p_b)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device=dev)
+    cu_q_t, cu_kv_t, pre, pk = i32(cu_q), i32(cu_kv), i32(S), i32(P)
+    bits_t = torch.tensor(np.array(bits, dtype=np.uint64).view(np.int64), device=dev)
+    rows = []
+    for dtype in (torch.float32, torch.bfloat16):
+        q, k, v = (torch.cat(x).to(dev, dtype) for x in (qs, ks, vs))
+        o_ref = ref_ta.varlen_tree_attention(q, k, v, cu_q_t, cu_kv_t, pre, pk, bits_t)
+        o_ours = cast_b200.varlen_tree_attention(q, k, v, cu_q_t, cu_kv_t, pre, pk, bits_t)
+        torch.cuda.synchronize()
+        if _lib.device_error() != 0:
+            raise RuntimeError("device error")
+        rows.append({"dtype": str(dtype).replace("torch.", ""),
+                     "max_abs_diff_ours_vs_ref": (o_ours.float() - o_ref.float()).abs().max().item(),
+                     "mean_abs_diff_ours_vs_ref": (o_ours.float() - o_ref.float()).abs().mean().item()})
+    print(json.dumps({"what": "vs_triton", "config": 0, "case": "reference test scenario (seed 0)", "rows": rows}))
+
+
 def vs_triton(args, dev):
     """This library's tree attention against the reference's Triton kernel on the same inputs."""
     import sys
@@ -89,6 +144,8 @@ def vs_triton(args, dev):
     dtypes = {"bf16": [torch.bfloat16], "fp16": [torch.float16], "fp32": [torch.float32]}[args.dtype]
     if args.config == 1:
         dtypes = [torch.float32, torch.bfloat16]
+    if args.config == 0:
+        return vs_triton_scenario(args, dev, ref_ta)
     base = workloads.config(args.config)
     if args.config == 5:
         base = workloads.with_width(base.shard(list(range(min(args.batch, base.B)))), args.width)
@@ -97,6 +154,10 @@ def vs_triton(args, dev):
     w = base
     assert max(w.P) <= 64, "the reference kernel takes packs of at most 64 tokens"
     lay = w.layout()
+    why = _ref_offsets_unsafe(lay["total_q"], lay["total_kv"], w.H_q, w.H_kv, w.D)
+    if why:
+        print(json.dumps({"what": "vs_triton", "config": args.config, "batch": w.B, "unavailable": why}))
+        return
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
     if args.config == 5:
         g = torch.Generator(device=dev).manual_seed(w.seed * 7919 + 17)

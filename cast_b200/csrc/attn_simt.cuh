@@ -48,6 +48,8 @@ struct AttnParams {
   // Limit of the tensor-core kernel's pipeline waits (ns). The waits that let
   // in-flight copies and MMAs drain before a CTA exits keep the full limit.
   uint64_t wait_ns;
+  // fp32 split path: flags[0..2] != 0 when the bf16 low parts of q / k / v hold any non-zero value
+  const int* split_flags;
 };
 
 // Key tiles of one sequence: the whole range for the regular layout, the

@@ -93,6 +93,36 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
+// The sequence of the given length rank (S + P descending, lower index first), computed by the
+// whole CTA from prefix_len / pack_len with `keys` (p.B ints of shared memory not yet used by any
+// TMA copy) as scratch; batches above kMaxRankedSeqs keep sequence order. Every CTA computes the
+// same permutation, so the launch covers each sequence exactly once.
+__device__ __forceinline__ int ranked_sequence(const AttnParams& p, int rank, int* keys) {
+  __shared__ int seq_of_rank;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  if (p.B <= kMaxRankedSeqs) {
+    for (int i = tid; i < p.B; i += nt) {
+      const long long k = (long long)p.prefix_len[i] + p.pack_len[i];
+      keys[i] = (int)max(-1LL, min(k, 0x7fffffffLL));
+    }
+    __syncthreads();
+    for (int i = tid; i < p.B; i += nt) {
+      const int ki = keys[i];
+      int r = 0;
+      for (int j = 0; j < p.B; ++j) {
+        const int kj = keys[j];
+        r += (kj > ki || (kj == ki && j < i)) ? 1 : 0;
+      }
+      if (r == rank) seq_of_rank = i;
+    }
+  } else if (tid == 0) {
+    seq_of_rank = rank;
+  }
+  tc::fence_proxy_async_smem();   // the keys' generic-proxy writes are ordered before later TMA copies there
+  __syncthreads();
+  return seq_of_rank;
+}
+
 // STORE = false: K/V are [total_kv, H_kv, D] (tmK, tmV; tmKp/tmVp unused).
 // STORE = true: tmK/tmV map the per-request prefix stores [B, H_kv, S_max, D]
 // (4-D), tmKp/tmVp the pack K/V [total_q, H_kv, D].
@@ -123,31 +153,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   rest /= gridDim.z;
   const int h = rest % p.H_kv;
   const int rank = rest / p.H_kv;
-  __shared__ int seq_of_rank;
-  {
-    int* keys = reinterpret_cast<int*>(smem + SMEM_K);   // scratch before any TMA load lands there
-    if (p.B <= kMaxRankedSeqs) {
-      for (int i = tid; i < p.B; i += NT) {
-        const long long k = (long long)p.prefix_len[i] + p.pack_len[i];
-        keys[i] = (int)max(-1LL, min(k, 0x7fffffffLL));
-      }
-      __syncthreads();
-      for (int i = tid; i < p.B; i += NT) {
-        const int ki = keys[i];
-        int r = 0;
-        for (int j = 0; j < p.B; ++j) {
-          const int kj = keys[j];
-          r += (kj > ki || (kj == ki && j < i)) ? 1 : 0;
-        }
-        if (r == rank) seq_of_rank = i;
-      }
-    } else if (tid == 0) {
-      seq_of_rank = rank;
-    }
-    fence_proxy_async_smem();   // the keys' generic-proxy writes are ordered before the TMA copies into this area
-    __syncthreads();
-  }
-  const int b = seq_of_rank;
+  const int b = ranked_sequence(p, rank, reinterpret_cast<int*>(smem + SMEM_K));  // K ring as scratch
   SeqMeta m;
   if constexpr (STORE) {
     m.q0 = p.cu_q[b]; m.kv0 = 0; m.S = p.prefix_len[b]; m.P = p.pack_len[b];

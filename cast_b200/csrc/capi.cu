@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "attn_simt.cuh"
 #include "attn_tc.cuh"
+#include "attn_tc3.cuh"
 #include "tree_build.cuh"
 #include "verify_ops.cuh"
 
@@ -213,6 +214,99 @@ int launch_tc_maps(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st, 
   return CAST_OK;
 }
 
+// ---- fp32 through the tensor cores (three-term bf16 split) --------------------------
+// Launch plan: 128-row query tiles (one per CTA); keys split as for the 16-bit kernel.
+TcPlan plan_tc3(int B, int total_q, int H_q, int H_kv, int max_pack, int max_kv, int sms) {
+  TcPlan pl;
+  const int G = H_q / H_kv;
+  pl.m_blocks = (G * max_pack + tc3::BM - 1) / tc3::BM;
+  if (pl.m_blocks < 1) pl.m_blocks = 1;
+  pl.W = (max_pack + 63) / 64;
+  if (pl.W < 1) pl.W = 1;
+  const long long base = (long long)B * H_kv * pl.m_blocks;
+  const long long target = 4LL * (sms > 0 ? sms : 148);
+  const int kv = max_kv > 0 ? max_kv : 1;
+  int chunk = ((kv + tc3::BN - 1) / tc3::BN) * tc3::BN;
+  int n_split = 1;
+  while (base * n_split < target && chunk > 16 * tc3::BN) {
+    n_split *= 2;
+    chunk = (((kv + n_split - 1) / n_split + tc3::BN - 1) / tc3::BN) * tc3::BN;
+  }
+  n_split = (kv + chunk - 1) / chunk;
+  pl.n_split = n_split;
+  pl.chunk = chunk;
+  pl.ws_bytes = n_split > 1 ? (size_t)n_split * total_q * H_q * (tc3::D + 2) * sizeof(float) : 0;
+  return pl;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Workspace of the split path: [partials][q hi][q lo][k hi][k lo][v hi][v lo][flags].
+struct Split3Layout {
+  size_t part, q_hi, q_lo, k_hi, k_lo, v_hi, v_lo, flags, total;
+};
+Split3Layout split3_layout(size_t part_bytes, long long total_q, long long total_kv, int H_q, int H_kv) {
+  Split3Layout w;
+  const size_t qb = align256((size_t)total_q * H_q * 128 * 2), kb = align256((size_t)total_kv * H_kv * 128 * 2);
+  w.part = 0;
+  w.q_hi = align256(part_bytes);
+  w.q_lo = w.q_hi + qb;
+  w.k_hi = w.q_lo + qb;
+  w.k_lo = w.k_hi + kb;
+  w.v_hi = w.k_lo + kb;
+  w.v_lo = w.v_hi + kb;
+  w.flags = w.v_lo + kb;
+  w.total = w.flags + 256;
+  return w;
+}
+
+int launch_tc3(AttnParams& p, const TcPlan& pl, const Split3Layout& lay, char* ws, int sms, cudaStream_t st) {
+  int* flags = reinterpret_cast<int*>(ws + lay.flags);
+  if (cudaMemsetAsync(flags, 0, 16, st) != cudaSuccess) return CAST_ERR_LAUNCH;
+  auto bf = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(ws + off); };
+  tc3::SplitArgs sa{};
+  sa.t[0] = {static_cast<const float*>(p.q), p.total_q, p.sq_m, p.sq_h, p.H_q, bf(lay.q_hi), bf(lay.q_lo)};
+  sa.t[1] = {static_cast<const float*>(p.k), p.total_kv, p.sk_m, p.sk_h, p.H_kv, bf(lay.k_hi), bf(lay.k_lo)};
+  sa.t[2] = {static_cast<const float*>(p.v), p.total_kv, p.sv_m, p.sv_h, p.H_kv, bf(lay.v_hi), bf(lay.v_lo)};
+  sa.flags = flags;
+  const long long n4 = std::max((long long)p.total_q * p.H_q, (long long)p.total_kv * p.H_kv) * 32;
+  const unsigned gx = (unsigned)std::max(1LL, std::min((n4 + 255) / 256, 8LL * (sms > 0 ? sms : 148)));
+  tc3::split3_kernel<<<dim3(gx, 3), 256, 0, st>>>(sa);
+  if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
+  const int G = p.G;
+  const int64_t qr = (int64_t)p.H_q * 128, kr = (int64_t)p.H_kv * 128;
+  if (!make_map(&mqh, ws + lay.q_hi, CAST_BF16, p.total_q, p.H_q, qr, 128, G, tc3::BM / G) ||
+      !make_map(&mql, ws + lay.q_lo, CAST_BF16, p.total_q, p.H_q, qr, 128, G, tc3::BM / G) ||
+      !make_map(&mkh, ws + lay.k_hi, CAST_BF16, p.total_kv, p.H_kv, kr, 128, 1, tc3::BN) ||
+      !make_map(&mkl, ws + lay.k_lo, CAST_BF16, p.total_kv, p.H_kv, kr, 128, 1, tc3::BN) ||
+      !make_map(&mvh, ws + lay.v_hi, CAST_BF16, p.total_kv, p.H_kv, kr, 128, 1, tc3::BN) ||
+      !make_map(&mvl, ws + lay.v_lo, CAST_BF16, p.total_kv, p.H_kv, kr, 128, 1, tc3::BN))
+    return CAST_ERR_LAUNCH;
+  p.split_flags = flags;
+  p.n_split = pl.n_split;
+  p.chunk = pl.chunk;
+  p.m_tiles = pl.m_blocks;
+  p.W = pl.W;
+  const size_t smem = tc3::smem_bytes(G, pl.W);
+  cudaFuncSetAttribute(tc3::attn_tc3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  tc3::attn_tc3_kernel<<<dim3(pl.m_blocks, p.B * p.H_kv, pl.n_split), tc3::NT, smem, st>>>(p, mqh, mql, mkh, mkl,
+                                                                                           mvh, mvl);
+  if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  if (pl.n_split > 1) {
+    const long long warps = (long long)p.total_q * p.H_q;
+    attn_combine_kernel<float><<<(int)((warps * 32 + 255) / 256), 256, 0, st>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  }
+  return CAST_OK;
+}
+
+bool split3_strides_ok(const int64_t* st, const void* q, const void* k, const void* v, const void* out) {
+  for (int t = 0; t < 4; ++t)
+    if (st[3 * t + 2] != 1 || st[3 * t] % 4 != 0 || st[3 * t + 1] % 4 != 0) return false;
+  return aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(out, 16);
+}
+
 int launch_tc(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   const int G = p.G;
@@ -295,7 +389,7 @@ const char* cast_strerror(int status) {
     case CAST_ERR_DTYPE: return "unsupported dtype (expected float32, bfloat16 or float16)";
     case CAST_ERR_HEAD_DIM: return "unsupported head dim (expected 64 or 128)";
     case CAST_ERR_PACK: return "pack too large (max_pack above CAST_MAX_PACK) or too few ancestor words per row";
-    case CAST_ERR_WORKSPACE: return "workspace smaller than cast_tree_attn_workspace_size()";
+    case CAST_ERR_WORKSPACE: return "workspace smaller than cast_tree_attn_workspace_size() (CAST_F32_SPLIT: _size_kv(), 256-byte aligned)";
     case CAST_ERR_ALIGN: return "misaligned pointer or stride (base 16-byte aligned, row/head strides multiples of 4 elements, dim stride 1)";
     case CAST_ERR_TOPK: return "k out of range (1 <= k <= CAST_MAX_TOPK, k <= V) or L out of range";
     case CAST_ERR_LAUNCH: return "CUDA launch failed";
@@ -328,10 +422,21 @@ int cast_device_error(cast_stream_t stream) {
   return h;
 }
 
+size_t cast_tree_attn_workspace_size_kv(int dtype, int B, int total_q, int total_kv, int H_q, int H_kv, int D,
+                                        int max_pack, int max_kv) {
+  if (dtype != CAST_F32_SPLIT)
+    return cast_tree_attn_workspace_size(dtype, B, total_q, H_q, H_kv, D, max_pack, max_kv);
+  if (B <= 0 || total_q <= 0 || total_kv < 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0 || D != 128) return 0;
+  const TcPlan tp = plan_tc3(B, total_q, H_q, H_kv, max_pack, max_kv, sm_count());
+  return split3_layout(tp.ws_bytes, total_q, total_kv, H_q, H_kv).total;
+}
+
 size_t cast_tree_attn_workspace_size(int dtype, int B, int total_q, int H_q, int H_kv, int D,
                                      int max_pack, int max_kv) {
-  (void)dtype;
   if (B <= 0 || total_q <= 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0) return 0;
+  if (dtype == CAST_F32_SPLIT)
+    return cast_tree_attn_workspace_size_kv(dtype, B, total_q, (int)std::min<long long>((long long)B * max_kv, 0x7fffffffLL),
+                                            H_q, H_kv, D, max_pack, max_kv);
   const int sms = sm_count();
   const SimtPlan pl = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sms);
   size_t ws = pl.ws_bytes;
@@ -346,10 +451,19 @@ int cast_tree_attn_plan(int dtype, int B, int total_q, int H_q, int H_kv, int D,
                         const int64_t* strides, const void* q, const void* k, const void* v, const void* out,
                         int* plan) {
   if (!strides || !plan) return CAST_ERR_NULL;
-  if (dtype != CAST_F32 && dtype != CAST_BF16 && dtype != CAST_F16) return CAST_ERR_DTYPE;
+  if (dtype != CAST_F32 && dtype != CAST_BF16 && dtype != CAST_F16 && dtype != CAST_F32_SPLIT) return CAST_ERR_DTYPE;
   if (B < 0 || total_q < 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0) return CAST_ERR_SHAPE;
   if (D != 64 && D != 128) return CAST_ERR_HEAD_DIM;
   const int sms = sm_count();
+  if (dtype == CAST_F32_SPLIT) {
+    if (D != 128 || 128 % (H_q / H_kv) != 0) return CAST_ERR_HEAD_DIM;
+    if (!split3_strides_ok(strides, q, k, v, out)) return CAST_ERR_ALIGN;
+    const TcPlan tp = plan_tc3(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
+    plan[0] = 2;
+    plan[1] = tp.n_split;
+    plan[2] = tp.n_split > 1 ? 3 : 2;
+    return CAST_OK;
+  }
   if (tc_eligible(dtype, D, H_q / H_kv, strides, q, k, v, out)) {
     const TcPlan tp = plan_tc(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
     plan[0] = 1;
@@ -372,11 +486,12 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
                        int B, int total_q, int total_kv, int H_q, int H_kv, int D,
                        float sm_scale, int max_pack, int max_kv,
                        void* workspace, size_t workspace_bytes, cast_stream_t stream) {
-  if (dtype != CAST_F32 && dtype != CAST_BF16 && dtype != CAST_F16) return CAST_ERR_DTYPE;
+  if (dtype != CAST_F32 && dtype != CAST_BF16 && dtype != CAST_F16 && dtype != CAST_F32_SPLIT) return CAST_ERR_DTYPE;
   if (B < 0 || total_q < 0 || total_kv < 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0 || max_pack < 0 ||
       max_kv < 0)
     return CAST_ERR_SHAPE;
   if (D != 64 && D != 128) return CAST_ERR_HEAD_DIM;
+  if (dtype == CAST_F32_SPLIT && (D != 128 || 128 % (H_q / H_kv) != 0)) return CAST_ERR_HEAD_DIM;
   if (max_pack > CAST_MAX_PACK) return CAST_ERR_PACK;
   if (B == 0 || total_q == 0 || max_pack == 0) return CAST_OK;  // nothing to compute
   if (!q || !k || !v || !out || !strides || !cu_q || !cu_kv || !prefix_len || !pack_len) return CAST_ERR_NULL;
@@ -406,6 +521,18 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
   p.wait_ns = g_pipeline_wait_ns.load(std::memory_order_relaxed);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == CAST_F32_SPLIT) {
+    if (!split3_strides_ok(strides, q, k, v, out)) return CAST_ERR_ALIGN;
+    const TcPlan tp = plan_tc3(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
+    const Split3Layout lay = split3_layout(tp.ws_bytes, total_q, total_kv, H_q, H_kv);
+    if (!workspace || workspace_bytes < lay.total || !aligned(workspace, 256)) return CAST_ERR_WORKSPACE;
+    char* ws = static_cast<char*>(workspace);
+    if (tp.ws_bytes > 0) {
+      p.ws_o = reinterpret_cast<float*>(ws);
+      p.ws_ml = p.ws_o + (size_t)tp.n_split * total_q * H_q * D;
+    }
+    return launch_tc3(p, tp, lay, ws, sms, st);
+  }
   if (tc_eligible(dtype, D, p.G, strides, q, k, v, out)) {
     const TcPlan tp = plan_tc(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
     if (tp.ws_bytes > 0) {

@@ -13,6 +13,10 @@ both keyword-only and optional:
 * ``max_pack=`` / ``max_kv=``: host-side bounds of pack_len and
   prefix_len + pack_len. Given, the call needs no device-to-host read; omitted,
   they are read back once, as the reference reads cu_q back (tree_attn.py:128).
+* ``fp32_path=``: float32 inputs run on the tensor cores from a three-term
+  bf16 split of q, k, v and the probabilities (``"split"``, the default where
+  D = 128 and H_q / H_kv divides 128; within ~1e-5 of exact fp32 at
+  unit-scale inputs) or on the exact CUDA-core kernel (``"exact"``).
 """
 import ctypes
 import math
@@ -39,28 +43,42 @@ def _i32(t, device):
     return t if (t.dtype == torch.int32 and t.is_contiguous()) else t.to(torch.int32).contiguous()
 
 
-def workspace_size(dtype, B, total_q, H_q, H_kv, D, max_pack, max_kv):
-    return int(_lib.lib().cast_tree_attn_workspace_size(_DTYPES[dtype], B, total_q, H_q, H_kv, D,
-                                                        max_pack, max_kv))
+def _code(dtype, D=128, G=4, fp32_path="split"):
+    """C-ABI dtype code of a call: fp32 takes the split tensor-core path where it applies."""
+    if dtype == torch.float32 and fp32_path == "split" and D == 128 and 128 % G == 0:
+        return _lib.CAST_F32_SPLIT
+    if fp32_path not in ("split", "exact"):
+        raise ValueError(f"fp32_path must be 'split' or 'exact', not {fp32_path!r}")
+    return _DTYPES[dtype]
 
 
-def attention_plan(q, k, v, out, B, max_pack, max_kv):
+def workspace_size(dtype, B, total_q, H_q, H_kv, D, max_pack, max_kv, total_kv=None, fp32_path="split"):
+    code = _code(dtype, D, H_q // H_kv, fp32_path)
+    if total_kv is None:
+        return int(_lib.lib().cast_tree_attn_workspace_size(code, B, total_q, H_q, H_kv, D, max_pack, max_kv))
+    return int(_lib.lib().cast_tree_attn_workspace_size_kv(code, B, total_q, total_kv, H_q, H_kv, D, max_pack,
+                                                           max_kv))
+
+
+def attention_plan(q, k, v, out, B, max_pack, max_kv, fp32_path="split"):
     """(kernel, key splits, launches) that varlen_tree_attention would use.
 
-    kernel is "tcgen05" (tensor-core kernel) or "simt" (CUDA-core kernel).
+    kernel is "tcgen05" (tensor-core kernel), "tcgen05_split" (fp32 through the
+    tensor cores from the bf16 split) or "simt" (CUDA-core kernel).
     """
     total_q, H_q, D = q.shape
     strides = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride(), *out.stride())
     plan = (ctypes.c_int * 3)()
-    code = _lib.lib().cast_tree_attn_plan(_DTYPES[q.dtype], B, total_q, H_q, k.shape[1], D, max_pack, max_kv,
+    code = _lib.lib().cast_tree_attn_plan(_code(q.dtype, D, H_q // k.shape[1], fp32_path), B, total_q, H_q,
+                                          k.shape[1], D, max_pack, max_kv,
                                           ctypes.addressof(strides), q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                           out.data_ptr(), ctypes.addressof(plan))
     _lib.check(code, "cast_tree_attn_plan")
-    return ("tcgen05" if plan[0] == 1 else "simt"), int(plan[1]), int(plan[2])
+    return {0: "simt", 1: "tcgen05", 2: "tcgen05_split"}[plan[0]], int(plan[1]), int(plan[2])
 
 
 def varlen_tree_attention(q, k, v, cu_q, cu_kv, prefix_len, pack_len, ancestor_mask=None, sm_scale=None,
-                          *, parent=None, max_pack=None, max_kv=None, out=None, workspace=None):
+                          *, parent=None, max_pack=None, max_kv=None, out=None, workspace=None, fp32_path="split"):
     """q: [total_q, H_q, D], k/v: [total_kv, H_kv, D] -> [total_q, H_q, D] (q's dtype).
 
     cu_q / cu_kv: int32 [B+1] offsets of packs and of concat(prefix, pack).
@@ -99,13 +117,16 @@ def varlen_tree_attention(q, k, v, cu_q, cu_kv, prefix_len, pack_len, ancestor_m
     else:
         par = _i32(parent, dev)
         par_ptr = par.data_ptr()
-    ws_bytes = workspace_size(q.dtype, B, total_q, H_q, H_kv, D, max_pack, max_kv)
-    if ws_bytes > 0 and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes):
+    dcode = _code(q.dtype, D, H_q // H_kv, fp32_path)
+    ws_bytes = int(_lib.lib().cast_tree_attn_workspace_size_kv(dcode, B, total_q, total_kv, H_q, H_kv, D,
+                                                               max_pack, max_kv))
+    if ws_bytes > 0 and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes
+                         or workspace.data_ptr() % 256 != 0):
         workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     strides = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride(), *out.stride())
     stream = torch.cuda.current_stream(dev).cuda_stream
     code = _lib.lib().cast_tree_attn_fwd(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), _DTYPES[q.dtype], ctypes.addressof(strides),
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dcode, ctypes.addressof(strides),
         cu_q_t.data_ptr(), cu_kv_t.data_ptr(), prefix_t.data_ptr(), pack_t.data_ptr(),
         anc_ptr, wpr, par_ptr, B, total_q, total_kv, H_q, H_kv, D, float(sm_scale), int(max_pack), int(max_kv),
         workspace.data_ptr() if ws_bytes > 0 else None, ws_bytes, stream)

@@ -40,8 +40,16 @@ extern "C" {
 
 typedef void* cast_stream_t;  /* cudaStream_t */
 
-/* element types of q / k / v / out */
-enum cast_dtype { CAST_F32 = 0, CAST_BF16 = 1, CAST_F16 = 2 };
+/*
+ * element types of q / k / v / out. CAST_F32_SPLIT (no counterpart in the
+ * reference) is fp32 data computed on the tensor cores: q, k, v and the
+ * softmax probabilities are carried as bf16 hi + lo pairs and every product
+ * takes the three significant terms (hi*hi + hi*lo + lo*hi), which keeps the
+ * output within ~1e-5 of exact fp32 arithmetic at unit-scale inputs (the
+ * reference's fp32 path, tree_attn.py with fp32 copies from serving.py:68-71,
+ * is held to 1e-4). CAST_F32 is the exact CUDA-core path.
+ */
+enum cast_dtype { CAST_F32 = 0, CAST_BF16 = 1, CAST_F16 = 2, CAST_F32_SPLIT = 3 };
 
 enum cast_status {
   CAST_OK = 0,
@@ -50,7 +58,7 @@ enum cast_status {
   CAST_ERR_DTYPE = -3,        /* unknown dtype */
   CAST_ERR_HEAD_DIM = -4,     /* head dim not in {64, 128} */
   CAST_ERR_PACK = -5,         /* max_pack above CAST_MAX_PACK, or anc words too few */
-  CAST_ERR_WORKSPACE = -6,    /* workspace smaller than cast_tree_attn_workspace_size() */
+  CAST_ERR_WORKSPACE = -6,    /* workspace smaller than cast_tree_attn_workspace_size() (CAST_F32_SPLIT: _size_kv(), base 256-byte aligned) */
   CAST_ERR_ALIGN = -7,        /* a pointer or stride breaks the kernel's alignment rule */
   CAST_ERR_TOPK = -8,         /* k out of range [1, CAST_MAX_TOPK] or V < k */
   CAST_ERR_LAUNCH = -9,       /* the CUDA launch itself failed */
@@ -108,8 +116,12 @@ void cast_test_set_wait_limit_ns(uint64_t ns);
  * sees every prefix key and pack key j iff bit j of its ancestor bitset is set.
  *
  * q: [total_q, H_q, D], k/v: [total_kv, H_kv, D], out: [total_q, H_q, D]; all
- *   of `dtype`; strides[12] = element strides (row, head, dim) of q, k, v, out.
- *   The dim stride must be 1.
+ *   of `dtype` (float32 for CAST_F32_SPLIT); strides[12] = element strides
+ *   (row, head, dim) of q, k, v, out. The dim stride must be 1.
+ *   CAST_F32_SPLIT needs D = 128, H_q / H_kv dividing 128, row / head strides
+ *   that are multiples of 4 and 16-byte aligned bases, and a workspace of
+ *   cast_tree_attn_workspace_size_kv() bytes (it holds the bf16 hi / lo copies
+ *   of q, k and v, 4 bytes per element of each).
  * anc_words: int64 [total_q, anc_words_per_row] ancestor bitsets (bit j of word
  *   j/64), the reference's `ancestor_mask` when anc_words_per_row == 1; or NULL.
  * parent: int32 [total_q] pack-local parents (-1 for the root, parent[i] < i),
@@ -180,6 +192,15 @@ size_t cast_tree_attn_workspace_size(int dtype, int B, int total_q, int H_q, int
                                      int max_pack, int max_kv);
 
 /*
+ * The same, exact for CAST_F32_SPLIT, whose workspace grows with total_kv
+ * (cast_tree_attn_workspace_size bounds total_kv by B * max_kv there). Equal to
+ * cast_tree_attn_workspace_size for the other dtypes. No counterpart in the
+ * reference.
+ */
+size_t cast_tree_attn_workspace_size_kv(int dtype, int B, int total_q, int total_kv, int H_q, int H_kv, int D,
+                                        int max_pack, int max_kv);
+
+/*
  * Tree attention reading the prefix straight from a per-request KV store.
  * Replaces the ragged K/V assembly of cast_trees/serving.py:60-71 (every layer
  * copies each request's prefix from its store into one buffer, k_rag/v_rag,
@@ -216,9 +237,11 @@ size_t cast_tree_attn_store_workspace_size(int dtype, int B, int total_q, int H_
 
 /*
  * How cast_tree_attn_fwd would run for these arguments (pure host arithmetic):
- * plan[0] = 1 for the tcgen05 tensor-core kernel, 0 for the CUDA-core kernel;
+ * plan[0] = 1 for the tcgen05 tensor-core kernel, 0 for the CUDA-core kernel,
+ * 2 for the tcgen05 kernel of CAST_F32_SPLIT (after its split pass);
  * plan[1] = number of key-range splits; plan[2] = kernel launches per call
- * (2 when split partials are merged by the combine kernel).
+ * (2 when split partials are merged by the combine kernel; CAST_F32_SPLIT adds
+ * its split pass).
  */
 int cast_tree_attn_plan(int dtype, int B, int total_q, int H_q, int H_kv, int D, int max_pack, int max_kv,
                         const int64_t* strides, const void* q, const void* k, const void* v, const void* out,

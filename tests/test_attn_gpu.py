@@ -43,18 +43,24 @@ def _oracle(sc, dtype):
     return oattn.tree_attention(q, k, v, sc["cu_q"], sc["cu_kv"], sc["prefix"], sc["pack"], _words(sc))
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+# fp32 inputs run two kernels: the tensor-core path from the three-term bf16 split (the default)
+# and the exact CUDA-core kernel; both are held to 1e-4
+DTYPE_PATHS = [(torch.float32, "split"), (torch.float32, "exact"), (torch.bfloat16, "split")]
+
+
+@pytest.mark.parametrize("dtype,path", DTYPE_PATHS)
 @pytest.mark.parametrize("mode", ["bits", "parent"])
-def test_reference_scenario(cuda, dtype, mode):
+def test_reference_scenario(cuda, dtype, path, mode):
     # tests/test_tree_attn.py:11-37 scenario: B=8, 32/8 heads, D=128, S in [200,400), P in [2,64)
     sc = ragged_scenario(seed=0, B=8, Hq=32, Hkv=8, D=128, s_range=(200, 400), p_range=(2, 64))
-    got = _run(sc, dtype, cuda, mode).float().cpu()
+    got = _run(sc, dtype, cuda, mode, fp32_path=path).float().cpu()
     err = (got - _oracle(sc, dtype)).abs()
     assert err.max().item() < TOL[dtype], err.max().item()
     assert err.mean().item() < 5e-3
 
 
-def test_golden_config1_fp32(cuda, golden):
+@pytest.mark.parametrize("path", ["split", "exact"])
+def test_golden_config1_fp32(cuda, golden, path):
     g = golden("attn_cfg1.npz")
     w = workloads.config(1)
     q, k, v = w.make_qkv(cuda)
@@ -63,16 +69,18 @@ def test_golden_config1_fp32(cuda, golden):
     out = cast_b200.varlen_tree_attention(q, k, v, torch.from_numpy(lay["cu_q"]).to(cuda),
                                           torch.from_numpy(lay["cu_kv"]).to(cuda),
                                           torch.from_numpy(lay["prefix_len"]).to(cuda),
-                                          torch.from_numpy(lay["pack_len"]).to(cuda), None, parent=parent)
+                                          torch.from_numpy(lay["pack_len"]).to(cuda), None, parent=parent,
+                                          fp32_path=path)
     err = (out.cpu() - torch.from_numpy(g["out"])).abs().max().item()
     assert err < 1e-4, err
 
 
+@pytest.mark.parametrize("path", ["split", "exact"])
 @pytest.mark.parametrize("mode", ["bits", "parent"])
-def test_golden_ragged_fp32(cuda, golden, mode):
+def test_golden_ragged_fp32(cuda, golden, mode, path):
     g = golden("attn_ragged.npz")
     sc = ragged_scenario(int(g["seed"]))
-    got = _run(sc, torch.float32, cuda, mode).cpu()
+    got = _run(sc, torch.float32, cuda, mode, fp32_path=path).cpu()
     err = (got - torch.from_numpy(g["out"])).abs().max().item()
     assert err < 1e-4, err
 
@@ -106,23 +114,23 @@ def _tree_scenario(seed, B, S_list, P_list, Hq=32, Hkv=8, D=128, depth_cap=None)
                 parent=np.array(parents, np.int32))
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_wide_packs_multiword(cuda, dtype):
+@pytest.mark.parametrize("dtype,path", DTYPE_PATHS)
+def test_wide_packs_multiword(cuda, dtype, path):
     # P above 64 needs several ancestor words per token; the reference caps P at 64
     sc = _tree_scenario(5, 4, [300, 0, 1000, 77], [128, 257, 129, 1000])
-    got = _run(sc, dtype, cuda, "parent").float().cpu()
+    got = _run(sc, dtype, cuda, "parent", fp32_path=path).float().cpu()
     err = (got - _oracle(sc, dtype)).abs().max().item()
     assert err < TOL[dtype], err
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_long_prefix_split_kv(cuda, dtype):
+@pytest.mark.parametrize("dtype,path", DTYPE_PATHS)
+def test_long_prefix_split_kv(cuda, dtype, path):
     # few (sequence, head) pairs and a long prefix: the launch splits the keys
     sc = _tree_scenario(6, 2, [32768, 20000], [129, 17], Hq=32, Hkv=8)
     sc["q"] *= 0.5; sc["k"] *= 0.5; sc["v"] *= 0.5
     B, total_q = 2, int(sc["cu_q"][-1])
-    assert cast_b200.workspace_size(dtype, B, total_q, 32, 8, 128, 129, 32768 + 129) > 0
-    got = _run(sc, dtype, cuda, "parent").float().cpu()
+    assert cast_b200.workspace_size(dtype, B, total_q, 32, 8, 128, 129, 32768 + 129, fp32_path=path) > 0
+    got = _run(sc, dtype, cuda, "parent", fp32_path=path).float().cpu()
     err = (got - _oracle(sc, dtype)).abs().max().item()
     assert err < TOL[dtype], err
 

@@ -65,6 +65,25 @@ def test_workspace_size_is_host_arithmetic(L):
     assert L.cast_tree_attn_workspace_size(1, 2, 258, 30, 8, 128, 129, 32897) == 0   # bad heads
 
 
+def test_fp32_split_workspace_holds_the_hi_lo_copies(L):
+    # CAST_F32_SPLIT: 2 bytes of hi + 2 of lo for every element of q, k, v, plus the flags (and partials
+    # when the keys are split); the size without total_kv bounds it by B * max_kv
+    B, total_q, total_kv, Hq, Hkv = 64, 8192, 401408, 32, 8
+    exact = L.cast_tree_attn_workspace_size_kv(3, B, total_q, total_kv, Hq, Hkv, 128, 128, 8320)
+    assert exact >= 4 * 128 * (total_q * Hq + 2 * total_kv * Hkv)
+    assert exact < 4 * 128 * (total_q * Hq + 2 * total_kv * Hkv) + 4096
+    bound = L.cast_tree_attn_workspace_size(3, B, total_q, Hq, Hkv, 128, 128, 8320)
+    assert bound >= exact
+    # the other dtypes: the two size functions agree
+    for dt in (0, 1, 2):
+        assert (L.cast_tree_attn_workspace_size_kv(dt, 2, 258, 65794, 32, 8, 128, 129, 32897)
+                == L.cast_tree_attn_workspace_size(dt, 2, 258, 32, 8, 128, 129, 32897))
+    assert L.cast_tree_attn_workspace_size_kv(3, 2, 258, 100, 32, 8, 64, 129, 50) == 0     # D = 64: no split path
+    # host checks of the split path: D must be 128, the workspace must be given
+    assert _attn(L, dtype=3, D=64) == -4
+    assert _attn(L, dtype=3) == -10 or _attn(L, dtype=3) == -6     # no device here, or no workspace
+
+
 def test_tree_argument_checks(L):
     p = 1 << 12
     assert L.cast_block_topk(None, 1, 10, 10, 2, p, p, None) == -1
