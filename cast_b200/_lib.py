@@ -31,7 +31,7 @@ EXPORTS = ("cast_strerror", "cast_version", "cast_device_error", "cast_tree_attn
            "cast_tree_attn_workspace_size", "cast_tree_attn_plan", "cast_block_topk", "cast_build_tree",
            "cast_tree_attn_fwd_noalloc", "cast_tree_attn_store_fwd", "cast_tree_attn_store_workspace_size",
            "cast_tree_walk_greedy", "cast_select_global_topk", "cast_append_store", "cast_gather_cache",
-           "cast_test_set_wait_limit_ns", "cast_tree_attn_workspace_size_kv")
+           "cast_test_set_wait_limit_ns", "cast_tree_attn_workspace_size_kv", "cast_kv_ragged_gather")
 CAST_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 
@@ -105,6 +105,10 @@ def lib():
     L.cast_tree_attn_plan.argtypes = [c_int] * 8 + [c_vp] * 6
     L.cast_tree_attn_workspace_size.restype = c_sz
     L.cast_tree_attn_workspace_size.argtypes = [c_int] * 8
+    L.cast_kv_ragged_gather.restype = c_int
+    L.cast_kv_ragged_gather.argtypes = [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp,
+                                        c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_i64, c_vp, c_vp, c_vp,
+                                        c_vp]
     L.cast_tree_attn_workspace_size_kv.restype = c_sz
     L.cast_tree_attn_workspace_size_kv.argtypes = [c_int] * 9
     L.cast_block_topk.restype = c_int

@@ -47,12 +47,128 @@ __host__ __device__ inline size_t smem_bytes(int G, int W) {
 
 // ---- split pass -----------------------------------------------------------------
 struct SplitSrc {
-  const float* src;      // [rows, heads, 128], dim stride 1
+  const float* src;      // [rows, heads, 128], dim stride 1 (store layout: [batch, heads, store_rows, 128])
   int64_t rows, s_row, s_head;
   int heads;
   __nv_bfloat16* hi;     // [rows, heads, 128] contiguous
   __nv_bfloat16* lo;
+  // Store layout (the store entry point's k and v): output row r is position s = r - cu_kv[b] of
+  // sequence b, read from the store at [b, h, s] for s < prefix_len[b] and from `pack`
+  // [cu_q[b] + s - prefix_len[b], h] after it; rows past cu_kv[B] are written as zeros.
+  int store;
+  const float* pack;
+  int64_t s_b, pk_row, pk_head;
+  int B, store_rows, max_pack, total_q;
+  const int32_t* cu_kv;
+  const int32_t* cu_q;
+  const int32_t* prefix_len;
+  const int32_t* pack_len;
 };
+
+// Largest b in [0, B) with cu[b] <= r (cu non-decreasing, cu[0] = 0).
+__device__ __forceinline__ int seq_of_row(const int32_t* cu, int B, int64_t r) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= r) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Source row (nullptr: write zeros) of ragged row r, head h of a store-layout tensor.
+__device__ __forceinline__ const float* store_row(const SplitSrc& t, int64_t r, int h) {
+  if (r >= t.cu_kv[t.B]) return nullptr;
+  const int b = seq_of_row(t.cu_kv, t.B, r);
+  const int64_t s = r - t.cu_kv[b];
+  const int S = t.prefix_len[b], P = t.pack_len[b], q0 = t.cu_q[b];
+  if (S < 0 || S > t.store_rows || P < 0 || P > t.max_pack || q0 < 0 || (int64_t)q0 + P > t.total_q || s < 0 ||
+      s >= (int64_t)S + P) {
+    report(CAST_DEV_BAD_LAYOUT);
+    return nullptr;
+  }
+  return s < S ? t.src + b * t.s_b + h * t.s_head + s * t.s_row : t.pack + (q0 + s - S) * t.pk_row + h * t.pk_head;
+}
+
+// cu_kv[b] = sum over b' < b of prefix_len[b'] + pack_len[b'] (negative lengths count as 0,
+// the sum saturates at INT32_MAX). One block of 1024 threads.
+__global__ void __launch_bounds__(1024) cu_kv_scan_kernel(const int32_t* prefix_len, const int32_t* pack_len, int B,
+                                                          int32_t* cu_kv) {
+  __shared__ long long warp_sum[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  long long carry = 0;
+  for (int base = 0; base < B; base += 1024) {
+    const int i = base + threadIdx.x;
+    long long x = i < B ? (long long)max(0, prefix_len[i]) + max(0, pack_len[i]) : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sum[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+      long long w = warp_sum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sum[lane] = w;
+    }
+    __syncthreads();
+    const long long incl = carry + x + (wid > 0 ? warp_sum[wid - 1] : 0);
+    if (i < B) cu_kv[i + 1] = (int32_t)min(incl, 0x7fffffffLL);
+    carry += warp_sum[31];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) cu_kv[0] = 0;
+}
+// ---- ragged assembly -------------------------------------------------------------
+// K and V of the store layout copied into the ragged layout [rows_cap, H, D] (contiguous),
+// for the shapes the tensor-core kernels do not take (the CUDA-core kernel reads only the
+// ragged layout). One warp per (row, head); rows past cu_kv[B] are zeros.
+struct GatherArgs {
+  const void* store[2];
+  const void* pack[2];
+  void* out[2];
+  int64_t st_b[2], st_h[2], st_r[2], pk_t[2], pk_h[2];
+  int B, H, D, store_rows, max_pack, total_q;
+  int64_t rows_cap;
+  const int32_t* cu_kv;
+  const int32_t* cu_q;
+  const int32_t* prefix_len;
+  const int32_t* pack_len;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) kv_ragged_gather_kernel(const GatherArgs a) {
+  const int kv = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int64_t n = a.rows_cap * a.H;
+  T* out = static_cast<T*>(a.out[kv]);
+  for (int64_t rh = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; rh < n;
+       rh += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t r = rh / a.H;
+    const int h = (int)(rh - r * a.H);
+    const T* src = nullptr;
+    if (r < a.cu_kv[a.B]) {
+      const int b = seq_of_row(a.cu_kv, a.B, r);
+      const int64_t s = r - a.cu_kv[b];
+      const int S = a.prefix_len[b], P = a.pack_len[b], q0 = a.cu_q[b];
+      if (S < 0 || S > a.store_rows || P < 0 || P > a.max_pack || q0 < 0 || (int64_t)q0 + P > a.total_q || s < 0 ||
+          s >= (int64_t)S + P) {
+        if (lane == 0) report(CAST_DEV_BAD_LAYOUT);
+      } else if (s < S) {
+        src = static_cast<const T*>(a.store[kv]) + b * a.st_b[kv] + h * a.st_h[kv] + s * a.st_r[kv];
+      } else {
+        src = static_cast<const T*>(a.pack[kv]) + (q0 + s - S) * a.pk_t[kv] + h * a.pk_h[kv];
+      }
+    }
+    T* dst = out + rh * a.D;
+    for (int c = lane; c < a.D; c += 32) dst[c] = src ? src[c] : T(0);
+  }
+}
+
 struct SplitArgs {
   SplitSrc t[3];         // q, k, v
   int* flags;            // [3], zeroed before the launch
@@ -68,7 +184,13 @@ __global__ void __launch_bounds__(256) split3_kernel(const SplitArgs a) {
     const int c = (int)(i & 31) * 4;
     const int64_t r = rh / t.heads;
     const int h = (int)(rh - r * t.heads);
-    const float4 x = __ldg(reinterpret_cast<const float4*>(t.src + r * t.s_row + h * t.s_head + c));
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t.store) {
+      const float* row = store_row(t, r, h);   // warp-uniform: the 32 lanes of a warp share (r, h)
+      if (row != nullptr) x = __ldg(reinterpret_cast<const float4*>(row + c));
+    } else {
+      x = __ldg(reinterpret_cast<const float4*>(t.src + r * t.s_row + h * t.s_head + c));
+    }
     const __nv_bfloat162 h01 = __floats2bfloat162_rn(x.x, x.y), h23 = __floats2bfloat162_rn(x.z, x.w);
     const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
     const __nv_bfloat162 l01 = __floats2bfloat162_rn(x.x - f01.x, x.y - f01.y);

@@ -260,14 +260,22 @@ Split3Layout split3_layout(size_t part_bytes, long long total_q, long long total
   return w;
 }
 
-int launch_tc3(AttnParams& p, const TcPlan& pl, const Split3Layout& lay, char* ws, int sms, cudaStream_t st) {
-  int* flags = reinterpret_cast<int*>(ws + lay.flags);
-  if (cudaMemsetAsync(flags, 0, 16, st) != cudaSuccess) return CAST_ERR_LAUNCH;
+// Split sources of the regular layout: q, k and v read as [rows, heads, 128].
+tc3::SplitArgs plain_split_args(const AttnParams& p, const Split3Layout& lay, char* ws) {
   auto bf = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(ws + off); };
   tc3::SplitArgs sa{};
   sa.t[0] = {static_cast<const float*>(p.q), p.total_q, p.sq_m, p.sq_h, p.H_q, bf(lay.q_hi), bf(lay.q_lo)};
   sa.t[1] = {static_cast<const float*>(p.k), p.total_kv, p.sk_m, p.sk_h, p.H_kv, bf(lay.k_hi), bf(lay.k_lo)};
   sa.t[2] = {static_cast<const float*>(p.v), p.total_kv, p.sv_m, p.sv_h, p.H_kv, bf(lay.v_hi), bf(lay.v_lo)};
+  return sa;
+}
+
+// Split pass then the attention kernel (and the combine when the keys are split). p describes
+// the ragged layout the hi / lo copies are in (p.cu_kv, p.total_kv rows).
+int launch_tc3(AttnParams& p, const TcPlan& pl, const Split3Layout& lay, char* ws, tc3::SplitArgs sa, int sms,
+               cudaStream_t st) {
+  int* flags = reinterpret_cast<int*>(ws + lay.flags);
+  if (cudaMemsetAsync(flags, 0, 16, st) != cudaSuccess) return CAST_ERR_LAUNCH;
   sa.flags = flags;
   const long long n4 = std::max((long long)p.total_q * p.H_q, (long long)p.total_kv * p.H_kv) * 32;
   const unsigned gx = (unsigned)std::max(1LL, std::min((n4 + 255) / 256, 8LL * (sms > 0 ? sms : 148)));
@@ -531,7 +539,7 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
       p.ws_o = reinterpret_cast<float*>(ws);
       p.ws_ml = p.ws_o + (size_t)tp.n_split * total_q * H_q * D;
     }
-    return launch_tc3(p, tp, lay, ws, sms, st);
+    return launch_tc3(p, tp, lay, ws, plain_split_args(p, lay, ws), sms, st);
   }
   if (tc_eligible(dtype, D, p.G, strides, q, k, v, out)) {
     const TcPlan tp = plan_tc(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
@@ -579,6 +587,11 @@ int cast_tree_attn_fwd_noalloc(const void* q, const void* k, const void* v, void
 size_t cast_tree_attn_store_workspace_size(int dtype, int B, int total_q, int H_q, int H_kv, int D, int max_pack,
                                            int max_prefix) {
   if (dtype == CAST_F32 || D != 128 || B <= 0 || total_q <= 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0) return 0;
+  if (dtype == CAST_F32_SPLIT) {
+    const long long rows_cap = (long long)B * ((long long)max_prefix + max_pack);
+    const TcPlan tp = plan_tc3(B, total_q, H_q, H_kv, max_pack, max_prefix + max_pack, sm_count());
+    return align256((size_t)(B + 1) * sizeof(int32_t)) + split3_layout(tp.ws_bytes, total_q, rows_cap, H_q, H_kv).total;
+  }
   return plan_tc_store(B, total_q, H_q, H_kv, max_pack, max_prefix, sm_count()).ws_bytes;
 }
 
@@ -589,7 +602,7 @@ int cast_tree_attn_store_fwd(const void* q, const void* k_store, const void* v_s
                              int B, int total_q, int store_batch, int store_rows, int H_q, int H_kv, int D,
                              float sm_scale, int max_pack, int max_prefix,
                              void* workspace, size_t workspace_bytes, cast_stream_t stream) {
-  if (dtype != CAST_BF16 && dtype != CAST_F16) return CAST_ERR_DTYPE;
+  if (dtype != CAST_BF16 && dtype != CAST_F16 && dtype != CAST_F32_SPLIT) return CAST_ERR_DTYPE;
   if (B < 0 || total_q < 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0 || max_pack < 0 || max_prefix < 0 ||
       store_batch < 0 || store_rows < 0)
     return CAST_ERR_SHAPE;
@@ -610,10 +623,11 @@ int cast_tree_attn_store_fwd(const void* q, const void* k_store, const void* v_s
   const int64_t* skp = strides + 11;
   const int64_t* svp = strides + 14;
   const int64_t* so = strides + 17;
+  const int sm = dtype == CAST_F32_SPLIT ? 4 : 8;   // stride multiple: 16 bytes either way
   for (const int64_t* t3 : {sq, skp, svp, so})
-    if (t3[2] != 1 || t3[0] % 8 != 0 || t3[1] % 8 != 0) return CAST_ERR_ALIGN;
+    if (t3[2] != 1 || t3[0] % sm != 0 || t3[1] % sm != 0) return CAST_ERR_ALIGN;
   for (const int64_t* t4 : {sks, svs})
-    if (t4[3] != 1 || t4[0] % 8 != 0 || t4[1] % 8 != 0 || t4[2] % 8 != 0) return CAST_ERR_ALIGN;
+    if (t4[3] != 1 || t4[0] % sm != 0 || t4[1] % sm != 0 || t4[2] % sm != 0) return CAST_ERR_ALIGN;
   if (!aligned(q, 16) || !aligned(k_store, 16) || !aligned(v_store, 16) || !aligned(k_pack, 16) ||
       !aligned(v_pack, 16) || !aligned(out, 16))
     return CAST_ERR_ALIGN;
@@ -634,6 +648,53 @@ int cast_tree_attn_store_fwd(const void* q, const void* k_store, const void* v_s
   p.max_pack = max_pack; p.max_kv = max_prefix + max_pack;
   p.store_mode = 1; p.store_rows = store_rows; p.store_batch = store_batch;
   p.wait_ns = g_pipeline_wait_ns.load(std::memory_order_relaxed);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  if (dtype == CAST_F32_SPLIT) {
+    // fp32: the split pass reads each prefix from its store and the pack rows from the pack
+    // tensors and writes the hi / lo copies in the ragged layout (cu_kv from a scan of the
+    // lengths, rows_cap = B * (max_prefix + max_pack) rows, unused rows zero); the attention
+    // kernel then runs on that layout.
+    const long long rows_cap = (long long)B * ((long long)max_prefix + max_pack);
+    if (rows_cap > 0x7fffffffLL) return CAST_ERR_SHAPE;
+    const TcPlan tp = plan_tc3(B, total_q, H_q, H_kv, max_pack, max_prefix + max_pack, sms);
+    const size_t cu_bytes = align256((size_t)(B + 1) * sizeof(int32_t));
+    const Split3Layout lay = split3_layout(tp.ws_bytes, total_q, rows_cap, H_q, H_kv);
+    if (!workspace || workspace_bytes < cu_bytes + lay.total || !aligned(workspace, 256)) return CAST_ERR_WORKSPACE;
+    int32_t* cu_kv = static_cast<int32_t*>(workspace);
+    char* ws = static_cast<char*>(workspace) + cu_bytes;
+    tc3::cu_kv_scan_kernel<<<1, 1024, 0, st>>>(prefix_len, pack_len, B, cu_kv);
+    if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+    p.store_mode = 0;
+    p.cu_kv = cu_kv;
+    p.total_kv = (int)rows_cap;
+    if (tp.ws_bytes > 0) {
+      p.ws_o = reinterpret_cast<float*>(ws);
+      p.ws_ml = p.ws_o + (size_t)tp.n_split * total_q * H_q * D;
+    }
+    tc3::SplitArgs sa{};
+    auto bf = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(ws + off); };
+    sa.t[0] = {static_cast<const float*>(q), total_q, sq[0], sq[1], H_q, bf(lay.q_hi), bf(lay.q_lo)};
+    const void* stores[2] = {k_store, v_store};
+    const void* packs[2] = {k_pack, v_pack};
+    const int64_t* sst[2] = {sks, svs};
+    const int64_t* spk[2] = {skp, svp};
+    const size_t his[2] = {lay.k_hi, lay.v_hi}, los[2] = {lay.k_lo, lay.v_lo};
+    for (int kv = 0; kv < 2; ++kv) {
+      tc3::SplitSrc& t = sa.t[1 + kv];
+      t.src = static_cast<const float*>(stores[kv]);
+      t.rows = rows_cap;
+      t.s_b = sst[kv][0]; t.s_head = sst[kv][1]; t.s_row = sst[kv][2];
+      t.heads = H_kv;
+      t.hi = bf(his[kv]); t.lo = bf(los[kv]);
+      t.store = 1;
+      t.pack = static_cast<const float*>(packs[kv]);
+      t.pk_row = spk[kv][0]; t.pk_head = spk[kv][1];
+      t.B = B; t.store_rows = store_rows; t.max_pack = max_pack; t.total_q = total_q;
+      t.cu_kv = cu_kv; t.cu_q = cu_q; t.prefix_len = prefix_len; t.pack_len = pack_len;
+    }
+    return launch_tc3(p, tp, lay, ws, sa, sms, st);
+  }
 
   const TcPlan pl = plan_tc_store(B, total_q, H_q, H_kv, max_pack, max_prefix, sms);
   if (pl.ws_bytes > 0) {
@@ -648,7 +709,46 @@ int cast_tree_attn_store_fwd(const void* q, const void* k_store, const void* v_s
       !make_map(&mkp, k_pack, dtype, total_q, H_kv, skp[0], skp[1], 1, tca::BN) ||
       !make_map(&mvp, v_pack, dtype, total_q, H_kv, svp[0], svp[1], 1, tca::BN))
     return CAST_ERR_LAUNCH;
-  return launch_tc_maps<true>(p, pl, dtype, static_cast<cudaStream_t>(stream), mq, mks, mvs, mkp, mvp);
+  return launch_tc_maps<true>(p, pl, dtype, st, mq, mks, mvs, mkp, mvp);
+}
+
+int cast_kv_ragged_gather(const void* k_store, const void* v_store, const void* k_pack, const void* v_pack,
+                          int elem_bytes, const int64_t* strides, const int32_t* cu_q, const int32_t* prefix_len,
+                          const int32_t* pack_len, int B, int total_q, int store_batch, int store_rows, int H, int D,
+                          int max_pack, int64_t rows_cap, void* k_out, void* v_out, int32_t* cu_kv_out,
+                          cast_stream_t stream) {
+  if (elem_bytes != 2 && elem_bytes != 4) return CAST_ERR_DTYPE;
+  if (B < 0 || total_q < 0 || store_batch < B || store_rows < 0 || H < 1 || D < 1 || max_pack < 0 || rows_cap < 0)
+    return CAST_ERR_SHAPE;
+  if (!cu_kv_out) return CAST_ERR_NULL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0) return cudaMemsetAsync(cu_kv_out, 0, sizeof(int32_t), st) == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
+  if (!k_store || !v_store || !k_pack || !v_pack || !strides || !cu_q || !prefix_len || !pack_len ||
+      (rows_cap > 0 && (!k_out || !v_out)))
+    return CAST_ERR_NULL;
+  // strides: k_store (4), v_store (4), k_pack (3), v_pack (3); dim strides 1
+  if (strides[3] != 1 || strides[7] != 1 || strides[10] != 1 || strides[13] != 1) return CAST_ERR_ALIGN;
+  tc3::cu_kv_scan_kernel<<<1, 1024, 0, st>>>(prefix_len, pack_len, B, cu_kv_out);
+  if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  if (rows_cap == 0) return CAST_OK;
+  tc3::GatherArgs a{};
+  a.store[0] = k_store; a.store[1] = v_store;
+  a.pack[0] = k_pack; a.pack[1] = v_pack;
+  a.out[0] = k_out; a.out[1] = v_out;
+  for (int kv = 0; kv < 2; ++kv) {
+    const int64_t* s4 = strides + 4 * kv;
+    const int64_t* s3 = strides + 8 + 3 * kv;
+    a.st_b[kv] = s4[0]; a.st_h[kv] = s4[1]; a.st_r[kv] = s4[2];
+    a.pk_t[kv] = s3[0]; a.pk_h[kv] = s3[1];
+  }
+  a.B = B; a.H = H; a.D = D; a.store_rows = store_rows; a.max_pack = max_pack; a.total_q = total_q;
+  a.rows_cap = rows_cap; a.cu_kv = cu_kv_out; a.cu_q = cu_q; a.prefix_len = prefix_len; a.pack_len = pack_len;
+  const int sms = sm_count();
+  const long long warps = rows_cap * H;
+  const unsigned gx = (unsigned)std::max(1LL, std::min((warps * 32 + 255) / 256, 16LL * (sms > 0 ? sms : 148)));
+  if (elem_bytes == 2) tc3::kv_ragged_gather_kernel<uint16_t><<<dim3(gx, 2), 256, 0, st>>>(a);
+  else tc3::kv_ragged_gather_kernel<uint32_t><<<dim3(gx, 2), 256, 0, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
 }
 
 int cast_block_topk(const double* logits, int64_t n_rows, int64_t V, int64_t row_stride, int k,

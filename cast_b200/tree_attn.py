@@ -134,14 +134,15 @@ def varlen_tree_attention(q, k, v, cu_q, cu_kv, prefix_len, pack_len, ancestor_m
     return out
 
 
-def _store_ready(t, rank):
+def _store_ready(t, mult):
+    """dim stride 1, other strides multiples of `mult` elements (16 bytes), 16-byte aligned base."""
     st = t.stride()
-    return st[-1] == 1 and all(x % 8 == 0 for x in st[:-1]) and t.data_ptr() % 16 == 0
+    return st[-1] == 1 and all(x % mult == 0 for x in st[:-1]) and t.data_ptr() % 16 == 0
 
 
 def varlen_tree_attention_store(q, k_store, v_store, k_pack, v_pack, cu_q, prefix_len, pack_len,
                                 ancestor_mask=None, sm_scale=None, *, parent=None, max_pack=None, max_prefix=None,
-                                out=None, workspace=None):
+                                out=None, workspace=None, fp32_path="split"):
     """Tree attention with each request's prefix read in place from its KV store.
 
     q: [total_q, H_q, D]; k_store / v_store: [B_store, H_kv, S_max, D], request
@@ -155,8 +156,10 @@ def varlen_tree_attention_store(q, k_store, v_store, k_pack, v_pack, cu_q, prefi
     the pack tensors.
 
     16-bit inputs with D = 128 and H_q / H_kv dividing 128 run the tensor-core
-    kernel directly; other inputs are assembled into the ragged layout on the
-    device (as the reference hook does) and run through varlen_tree_attention.
+    kernel directly; fp32 inputs of that shape run the split tensor-core path,
+    whose split pass reads the stores in place. Other inputs are assembled into
+    the ragged layout on the device (cast_kv_ragged_gather: no host read, no
+    per-request loop) and run through varlen_tree_attention.
     """
     total_q, H_q, D = q.shape
     Bs, H_kv, S_max, _ = k_store.shape
@@ -167,6 +170,8 @@ def varlen_tree_attention_store(q, k_store, v_store, k_pack, v_pack, cu_q, prefi
         raise RuntimeError("cast_b200.varlen_tree_attention_store needs CUDA tensors (no CPU path)")
     if (ancestor_mask is None) == (parent is None):
         raise ValueError("pass exactly one of ancestor_mask and parent")
+    if q.dtype not in _DTYPES or any(t.dtype != q.dtype for t in (k_store, v_store, k_pack, v_pack)):
+        raise TypeError("q, the stores and the pack tensors must share one of float32, bfloat16, float16")
     dev = q.device
     B = int(pack_len.shape[0])
     cu_q_t, prefix_t, pack_t = _i32(cu_q, dev), _i32(prefix_len, dev), _i32(pack_len, dev)
@@ -175,32 +180,36 @@ def varlen_tree_attention_store(q, k_store, v_store, k_pack, v_pack, cu_q, prefi
     if max_prefix is None:
         max_prefix = int(prefix_t.max().item()) if B > 0 else 0
     G = H_q // H_kv
-    direct = (q.dtype in (torch.bfloat16, torch.float16) and D == 128 and 128 % G == 0 and
-              all(t.dtype == q.dtype for t in (k_store, v_store, k_pack, v_pack)) and
-              _store_ready(q, 3) and _store_ready(k_store, 4) and _store_ready(v_store, 4) and
-              _store_ready(k_pack, 3) and _store_ready(v_pack, 3))
+    code, mult = None, 8
+    if D == 128 and 128 % G == 0:
+        if q.dtype in (torch.bfloat16, torch.float16):
+            code = _DTYPES[q.dtype]
+        elif fp32_path == "split":
+            code, mult = _lib.CAST_F32_SPLIT, 4
     if out is None:
         out = torch.empty_like(q)
-    if not direct or not _store_ready(out, 3):
-        # assemble concat(prefix_b, pack_b) per request, then the regular kernel
-        S = prefix_t.cpu().tolist()
-        P = pack_t.cpu().tolist()
-        cq = cu_q_t.cpu().tolist()
-        cu_kv = [0]
-        for s_b, p_b in zip(S, P):
-            cu_kv.append(cu_kv[-1] + s_b + p_b)
-        k_rag = torch.empty((cu_kv[-1], H_kv, D), dtype=k_pack.dtype, device=dev)
+    direct = code is not None and all(_store_ready(t, mult) for t in (q, k_store, v_store, k_pack, v_pack, out))
+    L = _lib.lib()
+    if not direct:
+        # the ragged layout, assembled on the device, then the regular entry point
+        dim1 = lambda t: t if t.stride(-1) == 1 else t.contiguous()
+        k_store, v_store, k_pack, v_pack = dim1(k_store), dim1(v_store), dim1(k_pack), dim1(v_pack)
+        rows_cap = B * (max_prefix + max_pack)
+        k_rag = torch.empty((rows_cap, H_kv, D), dtype=q.dtype, device=dev)
         v_rag = torch.empty_like(k_rag)
-        for b in range(B):
-            a = cu_kv[b]
-            k_rag[a:a + S[b]] = k_store[b, :, :S[b]].transpose(0, 1)
-            v_rag[a:a + S[b]] = v_store[b, :, :S[b]].transpose(0, 1)
-            k_rag[a + S[b]:a + S[b] + P[b]] = k_pack[cq[b]:cq[b] + P[b]]
-            v_rag[a + S[b]:a + S[b] + P[b]] = v_pack[cq[b]:cq[b] + P[b]]
-        res = varlen_tree_attention(q, k_rag, v_rag, cu_q_t, torch.tensor(cu_kv, dtype=torch.int32, device=dev),
-                                    prefix_t, pack_t, ancestor_mask, sm_scale, parent=parent, max_pack=max_pack,
-                                    max_kv=max(s + p for s, p in zip(S, P)) if B else 0)
-        out.copy_(res)
+        cu_kv = torch.empty(B + 1, dtype=torch.int32, device=dev)
+        st14 = (ctypes.c_int64 * 14)(*k_store.stride(), *v_store.stride(), *k_pack.stride(), *v_pack.stride())
+        rc = L.cast_kv_ragged_gather(k_store.data_ptr(), v_store.data_ptr(), k_pack.data_ptr(), v_pack.data_ptr(),
+                                     q.element_size(), ctypes.addressof(st14), cu_q_t.data_ptr(), prefix_t.data_ptr(),
+                                     pack_t.data_ptr(), B, total_q, Bs, S_max, H_kv, D, int(max_pack), rows_cap,
+                                     k_rag.data_ptr(), v_rag.data_ptr(), cu_kv.data_ptr(),
+                                     torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(rc, "cast_kv_ragged_gather")
+        res = varlen_tree_attention(q, k_rag, v_rag, cu_q_t, cu_kv, prefix_t, pack_t, ancestor_mask, sm_scale,
+                                    parent=parent, max_pack=max_pack, max_kv=max_prefix + max_pack,
+                                    out=out if _kernel_ready(out) else None, fp32_path=fp32_path)
+        if res is not out:
+            out.copy_(res)
         return out
     anc_ptr, wpr, par_ptr = None, 0, None
     if ancestor_mask is not None:
@@ -209,16 +218,15 @@ def varlen_tree_attention_store(q, k_store, v_store, k_pack, v_pack, cu_q, prefi
     else:
         par = _i32(parent, dev)
         par_ptr = par.data_ptr()
-    L = _lib.lib()
-    ws_bytes = int(L.cast_tree_attn_store_workspace_size(_DTYPES[q.dtype], B, total_q, H_q, H_kv, D, max_pack,
-                                                         max_prefix))
-    if ws_bytes > 0 and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes):
+    ws_bytes = int(L.cast_tree_attn_store_workspace_size(code, B, total_q, H_q, H_kv, D, max_pack, max_prefix))
+    if ws_bytes > 0 and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes
+                         or workspace.data_ptr() % 256 != 0):
         workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     strides = (ctypes.c_int64 * 20)(*q.stride(), *k_store.stride(), *v_store.stride(), *k_pack.stride(),
                                     *v_pack.stride(), *out.stride())
     code = L.cast_tree_attn_store_fwd(
         q.data_ptr(), k_store.data_ptr(), v_store.data_ptr(), k_pack.data_ptr(), v_pack.data_ptr(), out.data_ptr(),
-        _DTYPES[q.dtype], ctypes.addressof(strides), cu_q_t.data_ptr(), prefix_t.data_ptr(), pack_t.data_ptr(),
+        code, ctypes.addressof(strides), cu_q_t.data_ptr(), prefix_t.data_ptr(), pack_t.data_ptr(),
         anc_ptr, wpr, par_ptr, B, total_q, Bs, S_max, H_q, H_kv, D, float(sm_scale), int(max_pack),
         int(max_prefix), workspace.data_ptr() if ws_bytes > 0 else None, ws_bytes,
         torch.cuda.current_stream(dev).cuda_stream)

@@ -212,10 +212,15 @@ size_t cast_tree_attn_workspace_size_kv(int dtype, int B, int total_q, int total
  * are rows [cu_q[b], cu_q[b] + pack_len[b]) of k_pack / v_pack [total_q, H_kv, D]
  * (the current pass's keys, already in pack order). Visibility, output and
  * parent / ancestor conventions are those of cast_tree_attn_fwd.
- * 16-bit inputs (CAST_BF16 / CAST_F16), D = 128, H_q / H_kv dividing 128.
+ * 16-bit inputs (CAST_BF16 / CAST_F16), or fp32 inputs and output with
+ * CAST_F32_SPLIT; D = 128, H_q / H_kv dividing 128.
  * strides[20] = element strides of q (row, head, dim), k_store (batch, head,
  * row, dim), v_store (same), k_pack (row, head, dim), v_pack, out; dim strides
- * 1, every other stride a multiple of 8 elements, bases 16-byte aligned.
+ * 1, every other stride a multiple of 16 bytes (8 16-bit or 4 fp32 elements),
+ * bases 16-byte aligned. CAST_F32_SPLIT reads the stores once in its split pass
+ * (prefix rows from the store, pack rows from k_pack / v_pack) into ragged
+ * bf16 hi / lo copies in the workspace (256-byte aligned), then runs the
+ * tensor-core kernel on them.
  * max_prefix bounds prefix_len[b] (<= store_rows); workspace as returned by
  * cast_tree_attn_store_workspace_size(). Store rows past prefix_len[b] are
  * never part of the result, whatever they hold (non-finite values included).
@@ -234,6 +239,27 @@ int cast_tree_attn_store_fwd(const void* q, const void* k_store, const void* v_s
 /* Bytes of workspace cast_tree_attn_store_fwd needs for these sizes (0 is possible). */
 size_t cast_tree_attn_store_workspace_size(int dtype, int B, int total_q, int H_q, int H_kv, int D, int max_pack,
                                            int max_prefix);
+
+/*
+ * The ragged K/V assembly of cast_trees/serving.py:60-69 on the device, for
+ * store-mode calls the tensor-core kernels do not take (other head dims or
+ * group sizes, strides that are not 16-byte multiples): k_out / v_out
+ * [rows_cap, H, D] (contiguous, elem_bytes 2 or 4) receive, for sequence b at
+ * rows [cu_kv[b], cu_kv[b + 1]), its prefix rows [0, prefix_len[b]) of store
+ * row b followed by its pack rows [cu_q[b], cu_q[b] + pack_len[b]) of k_pack /
+ * v_pack; cu_kv_out [B + 1] receives the offsets (a scan of the lengths, on
+ * the device: no host read). Rows from cu_kv[B] to rows_cap are zero.
+ * rows_cap >= sum of prefix_len + pack_len, e.g. B * (max_prefix + max_pack).
+ * strides[14] = element strides of k_store, v_store (batch, head, row, dim) and
+ * k_pack, v_pack (row, head, dim); dim strides 1. Lengths outside
+ * [0, store_rows] / [0, max_pack] are reported as CAST_DEV_BAD_LAYOUT and their
+ * rows written as zeros. No counterpart in the reference's API.
+ */
+int cast_kv_ragged_gather(const void* k_store, const void* v_store, const void* k_pack, const void* v_pack,
+                          int elem_bytes, const int64_t* strides, const int32_t* cu_q, const int32_t* prefix_len,
+                          const int32_t* pack_len, int B, int total_q, int store_batch, int store_rows, int H, int D,
+                          int max_pack, int64_t rows_cap, void* k_out, void* v_out, int32_t* cu_kv_out,
+                          cast_stream_t stream);
 
 /*
  * How cast_tree_attn_fwd would run for these arguments (pure host arithmetic):

@@ -56,13 +56,13 @@ def _oracle(c, dtype):
     return oattn.tree_attention(c["q"].to(dtype).float(), k, v, cu_q, cu_kv, S, P, words), k, v, cu_kv
 
 
-def _run_store(c, dev, dtype):
+def _run_store(c, dev, dtype, **kw):
     t = lambda a: torch.from_numpy(np.asarray(a)).to(dev)
     kp = c["kp_hm"].to(dev, dtype).transpose(0, 1)     # strided view, as the hook would pass it
     vp = c["vp_hm"].to(dev, dtype).transpose(0, 1)
     out = cast_b200.varlen_tree_attention_store(c["q"].to(dev, dtype), c["k_store"].to(dev, dtype),
                                                 c["v_store"].to(dev, dtype), kp, vp, t(c["cu_q"]), t(c["S"]),
-                                                t(c["P"]), None, parent=t(c["parent"]))
+                                                t(c["P"]), None, parent=t(c["parent"]), **kw)
     assert _lib.device_error() == 0
     return out
 
@@ -98,11 +98,75 @@ def test_store_head_groups_and_split_keys(cuda, Hq, Hkv):
     assert (got - ref).abs().max().item() < 2e-2
 
 
-def test_store_fp32_assembles_and_runs_the_regular_kernel(cuda):
-    c = _store_case(34, [100, 3], [10, 7], Hq=8, Hkv=2, poison=False)
+@pytest.mark.parametrize("path", ["split", "exact"])
+def test_store_fp32(cuda, path):
+    # fp32 as the reference hook passes it: the split path reads the stores in its split pass (rows past
+    # each prefix are non-finite and never read); the exact path assembles the ragged layout on the device
+    c = _store_case(34, [100, 3, 0, 1280, 4099], [10, 7, 130, 64, 1], Hq=8, Hkv=2)
+    got = _run_store(c, cuda, torch.float32, fp32_path=path).cpu()
+    ref, *_ = _oracle(c, torch.float32)
+    assert torch.isfinite(got).all()
+    assert (got - ref).abs().max().item() < 1e-4
+
+
+def test_store_fp32_split_with_key_splits(cuda):
+    c = _store_case(36, [20000, 9000], [129, 17])
     got = _run_store(c, cuda, torch.float32).cpu()
     ref, *_ = _oracle(c, torch.float32)
     assert (got - ref).abs().max().item() < 1e-4
+
+
+@pytest.mark.parametrize("D,Hq,Hkv", [(64, 8, 2), (128, 12, 4)])
+def test_store_shapes_outside_the_tensor_core_kernel(cuda, D, Hq, Hkv):
+    # head dim 64 / group size 3: assembled on the device (cast_kv_ragged_gather), then the CUDA-core kernel
+    c = _store_case(37, [300, 0, 129], [20, 33, 5], Hq=Hq, Hkv=Hkv, D=D)
+    got = _run_store(c, cuda, torch.bfloat16).float().cpu()
+    ref, *_ = _oracle(c, torch.bfloat16)
+    assert torch.isfinite(got).all()
+    assert (got - ref).abs().max().item() < 2e-2
+
+
+def test_store_with_unaligned_row_stride(cuda):
+    # a store whose row stride (132 elements) is not a 16-byte multiple: no TMA map, the device assembly
+    c = _store_case(38, [257, 40], [31, 129])
+    wide = torch.zeros(2, 8, c["k_store"].shape[2], 132, dtype=torch.bfloat16, device=cuda)
+    ks, vs = wide.clone(), wide.clone()
+    ks[..., :128] = c["k_store"].to(cuda, torch.bfloat16)
+    vs[..., :128] = c["v_store"].to(cuda, torch.bfloat16)
+    t = lambda a: torch.from_numpy(np.asarray(a)).to(cuda)
+    out = cast_b200.varlen_tree_attention_store(c["q"].to(cuda, torch.bfloat16), ks[..., :128], vs[..., :128],
+                                                c["kp_hm"].to(cuda, torch.bfloat16).transpose(0, 1),
+                                                c["vp_hm"].to(cuda, torch.bfloat16).transpose(0, 1), t(c["cu_q"]),
+                                                t(c["S"]), t(c["P"]), None, parent=t(c["parent"]))
+    assert _lib.device_error() == 0
+    ref, *_ = _oracle(c, torch.bfloat16)
+    assert (out.float().cpu() - ref).abs().max().item() < 2e-2
+
+
+def test_ragged_gather_layout(cuda):
+    import ctypes
+    c = _store_case(39, [5, 0, 130], [3, 2, 4], Hq=8, Hkv=2, D=64)
+    dev = cuda
+    t = lambda a: torch.from_numpy(np.asarray(a)).to(dev)
+    ks, vs = c["k_store"].to(dev), c["v_store"].to(dev)
+    kp, vp = c["kp_hm"].to(dev).transpose(0, 1), c["vp_hm"].to(dev).transpose(0, 1)
+    rows_cap = 3 * (130 + 4)
+    k_rag = torch.full((rows_cap, 2, 64), 7.0, device=dev)
+    v_rag = torch.full_like(k_rag, 7.0)
+    cu_kv = torch.empty(4, dtype=torch.int32, device=dev)
+    st = (ctypes.c_int64 * 14)(*ks.stride(), *vs.stride(), *kp.stride(), *vp.stride())
+    cu_q, S, P = t(c["cu_q"]), t(c["S"]), t(c["P"])    # held: the call takes raw device pointers
+    rc = _lib.lib().cast_kv_ragged_gather(ks.data_ptr(), vs.data_ptr(), kp.data_ptr(), vp.data_ptr(), 4,
+                                          ctypes.addressof(st), cu_q.data_ptr(), S.data_ptr(),
+                                          P.data_ptr(), 3, 9, 3, ks.shape[2], 2, 64, 4, rows_cap,
+                                          k_rag.data_ptr(), v_rag.data_ptr(), cu_kv.data_ptr(),
+                                          torch.cuda.current_stream().cuda_stream)
+    assert rc == 0 and _lib.device_error() == 0
+    _, k_ref, v_ref, cu_ref = _oracle(c, torch.float32)
+    n = int(cu_ref[-1])
+    assert cu_kv.cpu().tolist() == [int(x) for x in cu_ref]
+    assert torch.equal(k_rag[:n].cpu(), k_ref) and torch.equal(v_rag[:n].cpu(), v_ref)
+    assert torch.all(k_rag[n:] == 0) and torch.all(v_rag[n:] == 0)
 
 
 def test_store_with_ancestor_bits_as_the_hook_passes_them(cuda):
