@@ -6,8 +6,9 @@
 // key range [0, S_b + P_b) (the whole range unless the launch splits keys).
 //
 // Roles (12 warps):
-//   warp 0      TMEM allocation; lane 0 issues the TMA loads: the Q tiles once,
-//               then 128-key K and V tiles into a 2-stage ring.
+//   warp 0      TMEM allocation; one lane issues the TMA loads of the Q tiles (once)
+//               and of the 128-key K tiles into a 2-stage ring.
+//   warp 2      one lane issues the TMA loads of the V tiles into their 2-stage ring.
 //   warp 1      lane 0 issues every tcgen05.mma:
 //                 S_q  = Q_q K_j^T    (A, B in shared memory, K-major)
 //                 O_q += P_q V_j      (A = P in tensor memory, B = V MN-major)
@@ -242,10 +243,14 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   // Warps 0 and 1 walk their schedules converged, so warp-uniform values (loop
   // counters, shared-memory addresses, descriptors) stay in uniform registers;
   // one elected lane issues each TMA copy / MMA / commit.
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------ TMA producers
+    // Warp 0 loads the Q tiles and the K ring, warp 2 the V ring: a K slot frees up after the
+    // second QK of its tile, a V slot only after the second PV, so one loop over both would hold
+    // every K copy back behind the previous V slot.
+    const bool is_k = warp == 0;
     const uint32_t qf = smem_u32(&bars.q_full);
-    if (elect_one()) {
+    if (is_k && elect_one()) {
       mbar_expect_tx(qf, n_qt * TILE_BYTES);
       for (int q = 0; q < n_qt; ++q) {
         const int tok = m.q0 + (r_base + q * BM) / G;
@@ -254,13 +259,22 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
       }
     }
     __syncwarp();
-    int issued_k = 0, issued_v = 0;   // K / V tiles whose copies were issued
+    uint64_t* full = is_k ? bars.k_full : bars.v_full;
+    uint64_t* empty = is_k ? bars.k_empty : bars.v_empty;
+    const uint32_t ring = smem_u32(smem + (is_k ? SMEM_K : SMEM_V));
+    const CUtensorMap* m_reg = is_k ? &tmK : &tmV;
+    const CUtensorMap* m_pack = is_k ? &tmKp : &tmVp;
+    int issued = 0;   // tiles whose copies were issued
     for (int j = 0; j < n_kt; ++j) {
       const int s = j % NST;
       const uint32_t use = (uint32_t)(j / NST);
       const int row = m.kv0 + k_begin + j * BN;
-      // one 128-key tile of K or V (two 64-column halves) into the ring slot
-      auto load_tile = [&](const CUtensorMap* m_reg, const CUtensorMap* m_pack, uint32_t dst, uint32_t bar) {
+      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&empty[s]), (use - 1) & 1, abort_flag, p.wait_ns)))
+        break;
+      if (elect_one()) {
+        const uint32_t dst = ring + s * TILE_BYTES, bar = smem_u32(&full[s]);
+        mbar_expect_tx(bar, TILE_BYTES);
+        // one 128-key tile (two 64-column halves) into the ring slot
         for (int hf = 0; hf < 2; ++hf) {
           if constexpr (STORE) {
             const int t = t_begin + j;
@@ -270,31 +284,15 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
             tma_load_3d(dst + hf * HALF_BYTES, m_reg, hf * 64, h, row, bar);
           }
         }
-      };
-      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.k_empty[s]), (use - 1) & 1, abort_flag, p.wait_ns)))
-        break;
-      if (elect_one()) {
-        mbar_expect_tx(smem_u32(&bars.k_full[s]), TILE_BYTES);
-        load_tile(&tmK, &tmKp, smem_u32(smem + SMEM_K + s * TILE_BYTES), smem_u32(&bars.k_full[s]));
       }
       __syncwarp();
-      issued_k = j + 1;
-      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars.v_empty[s]), (use - 1) & 1, abort_flag, p.wait_ns)))
-        break;
-      if (elect_one()) {
-        mbar_expect_tx(smem_u32(&bars.v_full[s]), TILE_BYTES);
-        load_tile(&tmV, &tmVp, smem_u32(smem + SMEM_V + s * TILE_BYTES), smem_u32(&bars.v_full[s]));
-      }
-      __syncwarp();
-      issued_v = j + 1;
+      issued = j + 1;
     }
     // let the last copies land before the CTA can exit (immediate on the normal path); only
     // copies that were issued are waited for
-    for (int j = max(0, issued_k - NST); j < issued_k; ++j)
-      mbar_wait(smem_u32(&bars.k_full[j % NST]), (uint32_t)(j / NST) & 1, nullptr);
-    for (int j = max(0, issued_v - NST); j < issued_v; ++j)
-      mbar_wait(smem_u32(&bars.v_full[j % NST]), (uint32_t)(j / NST) & 1, nullptr);
-    mbar_wait(qf, 0, nullptr);
+    for (int j = max(0, issued - NST); j < issued; ++j)
+      mbar_wait(smem_u32(&full[j % NST]), (uint32_t)(j / NST) & 1, nullptr);
+    if (is_k) mbar_wait(qf, 0, nullptr);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false, false);

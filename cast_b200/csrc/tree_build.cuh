@@ -91,6 +91,34 @@ __device__ __forceinline__ double exp_fast_clamped(double t) {
   return p * __hiloint2double((k + 1023) << 20, 0);
 }
 
+// exp(t) in float64 for -708 <= t <= 709 from a 64-entry table (callers clamp): t = (64 n + i) ln2/64 + r
+// with |r| <= ln2/128 (Cody-Waite with the split ln 2 of exp_fast, scaled by 1/64, exact for |64 n + i|
+// < 2^20), e^t = 2^n * 2^(i/64) * e^r, e^r by its degree-5 Taylor polynomial (truncation < 4e-17
+// relative) and 2^n added to the exponent field of the table entry. Ten float64 operations against
+// exp_fast's sixteen; `tab` holds 2^(i/64), i = 0..63 (exp2_table_init).
+__device__ __forceinline__ double exp_tab(double t, const double* tab) {
+  constexpr double kScale = 92.33248261689366;            // 64 / ln 2
+  constexpr double kLn2Hi64 = 0.6931471803691238 / 64.0;  // exact: a power-of-two scale of exp_fast's split
+  constexpr double kLn2Lo64 = 1.9082149292705877e-10 / 64.0;
+  constexpr double kShift = 6755399441055744.0;           // 1.5 * 2^52
+  const double kd = fma(t, kScale, kShift);
+  const int m = __double2loint(kd);
+  const double kf = kd - kShift;
+  const double r = fma(-kf, kLn2Lo64, fma(-kf, kLn2Hi64, t));
+  double p = 1.0 / 120.0;
+  p = fma(p, r, 1.0 / 24.0);
+  p = fma(p, r, 1.0 / 6.0);
+  p = fma(p, r, 0.5);
+  p = fma(p, r, 1.0);
+  p = fma(p, r, 1.0);
+  const double tv = tab[m & 63];
+  return p * __hiloint2double(__double2hiint(tv) + ((m >> 6) << 20), __double2loint(tv));
+}
+
+__device__ __forceinline__ void exp2_table_init(double* tab) {
+  for (int i = threadIdx.x; i < 64; i += blockDim.x) tab[i] = exp2((double)i / 64.0);
+}
+
 // Folds one element into a thread's (reference, sum of exp(x - reference)).
 __device__ __forceinline__ void lse_add(double& ref, double& s, double v) {
   if (v == -INFINITY) return;
@@ -312,16 +340,20 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
   const double* x = logits + row * row_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+  __shared__ double s_tab[64];
+  exp2_table_init(s_tab);
+  __syncthreads();
   WarpCands<KC> wc{w_x[warp], w_i[warp], 0, -INFINITY, -1, false};
   double ref = -INFINITY, s = 0.0;
   // Elements of one batch; every lane runs the same number of batches (elements past the row
   // are -inf and invalid). The log-sum reference moves once per batch: when the batch max
   // exceeds it by more than 256, so every exp argument is at most 256.
-  // (arrays of 8 with constant indices after unrolling; entries past nb are ignored)
-  auto batch = [&](const double (&v)[8], const int (&j)[8], const bool (&ok)[8], int nb) {
+  // (arrays of 8 with constant indices after unrolling; entries past nb are ignored; index(u) gives
+  // the element's index and is evaluated only when an element enters the candidate buffer)
+  auto batch = [&](const double (&v)[8], auto&& index, const bool (&ok)[8], int nb, bool all_ok) {
     double mv[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) mv[u] = (u < nb && ok[u]) ? v[u] : -INFINITY;
+    for (int u = 0; u < 8; ++u) mv[u] = (u < nb && (all_ok || ok[u])) ? v[u] : -INFINITY;
     const double bm = fmax(fmax(fmax(mv[0], mv[1]), fmax(mv[2], mv[3])), fmax(fmax(mv[4], mv[5]), fmax(mv[6], mv[7])));
     if (bm != -INFINITY && !(bm - ref <= 256.0)) {
       s = (ref == -INFINITY) ? 0.0 : s * exp_fast(ref - bm);
@@ -331,57 +363,65 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
     // nothing next to a sum that holds a term of 1
     double e[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) e[u] = u < nb ? exp_fast_clamped(fmax(v[u] - ref, -708.0)) : 0.0;
+    for (int u = 0; u < 8; ++u) e[u] = u < nb ? exp_tab(fmax(v[u] - ref, -708.0), s_tab) : 0.0;
     s += ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));   // a tree: short dependency chain
+    // candidates: one vote per batch; the per-element offers (a ballot each, in element order) run
+    // only when some lane holds an element that clears the threshold as it stands at the batch start
+    // (the threshold only rises, so this admits a superset of what the offers take in)
+    bool any = false;
 #pragma unroll
     for (int u = 0; u < 8; ++u)
-      if (u < nb) wc.offer(v[u], j[u], ok[u]);
+      any |= u < nb && (all_ok || ok[u]) && (!wc.full || v[u] >= wc.tx);
+    if (__any_sync(0xffffffffu, any)) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (u < nb) wc.offer(v[u], index(u), all_ok || ok[u]);
+    }
   };
   if (VEC2) {
     const double2* x2 = reinterpret_cast<const double2*>(x);
     const int64_t n2 = V >> 1;
+    const int64_t n2_full = n2 - n2 % (4 * NT);   // batches every lane's loads stay inside
     for (int64_t base = 0; base < n2; base += 4 * NT) {
+      const bool full_batch = base < n2_full;
       double2 d[4];
       bool okp[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int64_t ii = base + u * NT + tid;
-        okp[u] = ii < n2;
+        okp[u] = full_batch || ii < n2;
         d[u] = okp[u] ? __ldcs(x2 + ii) : make_double2(-INFINITY, -INFINITY);
       }
       double v[8];
-      int j[8];
       bool ok[8];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int jj = (int)(2 * (base + u * NT + tid));
         v[2 * u] = d[u].x; v[2 * u + 1] = d[u].y;
-        j[2 * u] = jj; j[2 * u + 1] = jj + 1;
         ok[2 * u] = okp[u]; ok[2 * u + 1] = okp[u];
       }
-      batch(v, j, ok, 8);
+      auto index = [&](int u) { return (int)(2 * (base + (u >> 1) * NT + tid)) + (u & 1); };
+      batch(v, index, ok, 8, full_batch);
     }
     if (V & 1) {   // the odd last element: lane 0 of warp 0, the warp calls together
       if (warp == 0) {
         double v[8] = {lane == 0 ? x[V - 1] : -INFINITY};
-        int j[8] = {(int)(V - 1)};
         bool ok[8] = {lane == 0};
-        batch(v, j, ok, 1);
+        auto index = [&](int) { return (int)(V - 1); };
+        batch(v, index, ok, 1, false);
       }
     }
   } else {
     for (int64_t base = 0; base < V; base += 8 * NT) {
       double v[8];
-      int j[8];
       bool ok[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int64_t ii = base + u * NT + tid;
         ok[u] = ii < V;
         v[u] = ok[u] ? x[ii] : -INFINITY;
-        j[u] = (int)ii;
       }
-      batch(v, j, ok, 8);
+      auto index = [&](int u) { return (int)(base + u * NT + tid); };
+      batch(v, index, ok, 8, false);
     }
   }
   wc.cut();   // the warp's KC best, in order
@@ -544,7 +584,8 @@ __host__ __device__ inline size_t tree_smem_bytes(int max_budget, int L, int k) 
   return nc * (2 * sizeof(uint64_t) + sizeof(double) + 4 * sizeof(int)) +  // candidates
          (size_t)max_budget * sizeof(double) +                            // node neg
          ((size_t)max_budget + 1) * k * sizeof(unsigned char) +            // child order per node (+root)
-         (size_t)L * k * sizeof(double) + 64;                              // lp rows
+         (size_t)L * k * sizeof(double) +                                  // lp rows
+         (size_t)L * k * sizeof(int32_t) + 64;                             // token rows
 }
 
 // Warp-wide arg-min of a 128-bit key (hi, lo); every lane returns the winner's
@@ -579,7 +620,8 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
   int* c_r = c_d + nc_max;                              // rank
   double* n_neg = reinterpret_cast<double*>(c_r + nc_max);
   double* s_lp = n_neg + a.max_budget;
-  unsigned char* order = reinterpret_cast<unsigned char*>(s_lp + (size_t)L * k);  // [(1 + max_budget)][k], row 0 = root
+  int32_t* s_tok = reinterpret_cast<int32_t*>(s_lp + (size_t)L * k);                // token of each (row, rank)
+  unsigned char* order = reinterpret_cast<unsigned char*>(s_tok + (size_t)L * k);  // [(1 + max_budget)][k], row 0 = root
 
   int budget = a.budget[b];
   if (budget > a.max_budget || budget < 0) {
@@ -589,9 +631,11 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
   const double* lp_g = a.top_lp + (size_t)b * L * a.k_cols;
   const int64_t* idx_g = a.top_idx + (size_t)b * L * a.k_cols;
   bool sorted_rows = true;
+  // the tree's lp and token tables, staged once: no global load on the pop loop's dependency chain
   for (int e = lane; e < L * k; e += 32) {
     const double v = lp_g[(e / k) * a.k_cols + (e % k)];
     s_lp[e] = v;
+    s_tok[e] = (int32_t)idx_g[(e / k) * a.k_cols + (e % k)];
     if (e % k != k - 1 && !(v >= lp_g[(e / k) * a.k_cols + (e % k) + 1])) sorted_rows = false;
   }
   // Rows sorted best-first (block_topk's output): fl(neg - lp[d, r]) is then
@@ -631,6 +675,7 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
 
   int n = 0;
   const int q0 = a.cu_q ? a.cu_q[b] : 0;
+  const int pos0 = (a.cu_q && a.pack_pos) ? a.seq_len[b] : 0;
   bool pack_ok = true;
   if (a.cu_q && lane == 0) {
     pack_ok = q0 >= 0 && (long long)q0 + 1 + budget <= (long long)a.cu_q[b + 1];
@@ -652,7 +697,7 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
     const int me = n;
     __syncwarp();  // every lane has read the slot before lane 0 rewrites it
     if (lane == 0) {
-      const int tok = (int)idx_g[(size_t)(d - 1) * a.k_cols + r];
+      const int tok = s_tok[(size_t)(d - 1) * k + r];
       const size_t o = (size_t)b * a.max_budget + me;
       a.token[o] = tok;
       a.depth[o] = d;
@@ -662,7 +707,7 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
       if (a.cu_q && pack_ok) {
         if (a.pack_parent) a.pack_parent[q0 + 1 + me] = par + 1;
         if (a.pack_token) a.pack_token[q0 + 1 + me] = tok;
-        if (a.pack_pos) a.pack_pos[q0 + 1 + me] = a.seq_len[b] + d;
+        if (a.pack_pos) a.pack_pos[q0 + 1 + me] = pos0 + d;
       }
       // the popped slot takes the next sibling, or the last candidate
       if (j + 1 < k) {
@@ -699,7 +744,7 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
     if (a.cu_q && pack_ok) {
       if (a.pack_parent) a.pack_parent[q0] = -1;
       if (a.pack_token) a.pack_token[q0] = a.root_token[b];
-      if (a.pack_pos) a.pack_pos[q0] = a.seq_len[b];
+      if (a.pack_pos) a.pack_pos[q0] = pos0;
     }
   }
 }
