@@ -3,6 +3,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace cast {
 
@@ -96,21 +97,25 @@ __device__ __forceinline__ double exp_fast_clamped(double t) {
 // < 2^20), e^t = 2^n * 2^(i/64) * e^r, e^r by its degree-5 Taylor polynomial (truncation < 4e-17
 // relative) and 2^n added to the exponent field of the table entry. Ten float64 operations against
 // exp_fast's sixteen; `tab` holds 2^(i/64), i = 0..63 (exp2_table_init).
+// The constants live in the constant bank, where an fp64 instruction reads them as an operand: as
+// literals they were rebuilt from two 32-bit moves at every use under the kernel's register budget.
+__constant__ double c_exp_tab[9] = {
+    92.33248261689366,             // 64 / ln 2
+    6755399441055744.0,            // 1.5 * 2^52
+    -0.6931471803691238 / 64.0,    // -(ln 2 head) / 64, exact: a power-of-two scale of exp_fast's split
+    -1.9082149292705877e-10 / 64.0,
+    1.0 / 120.0, 1.0 / 24.0, 1.0 / 6.0, 0.5, 1.0};
 __device__ __forceinline__ double exp_tab(double t, const double* tab) {
-  constexpr double kScale = 92.33248261689366;            // 64 / ln 2
-  constexpr double kLn2Hi64 = 0.6931471803691238 / 64.0;  // exact: a power-of-two scale of exp_fast's split
-  constexpr double kLn2Lo64 = 1.9082149292705877e-10 / 64.0;
-  constexpr double kShift = 6755399441055744.0;           // 1.5 * 2^52
-  const double kd = fma(t, kScale, kShift);
+  const double kd = fma(t, c_exp_tab[0], c_exp_tab[1]);
   const int m = __double2loint(kd);
-  const double kf = kd - kShift;
-  const double r = fma(-kf, kLn2Lo64, fma(-kf, kLn2Hi64, t));
-  double p = 1.0 / 120.0;
-  p = fma(p, r, 1.0 / 24.0);
-  p = fma(p, r, 1.0 / 6.0);
-  p = fma(p, r, 0.5);
-  p = fma(p, r, 1.0);
-  p = fma(p, r, 1.0);
+  const double kf = kd - c_exp_tab[1];
+  const double r = fma(kf, c_exp_tab[3], fma(kf, c_exp_tab[2], t));
+  double p = c_exp_tab[4];
+  p = fma(p, r, c_exp_tab[5]);
+  p = fma(p, r, c_exp_tab[6]);
+  p = fma(p, r, c_exp_tab[7]);
+  p = fma(p, r, c_exp_tab[8]);
+  p = fma(p, r, c_exp_tab[8]);
   const double tv = tab[m & 63];
   return p * __hiloint2double(__double2hiint(tv) + ((m >> 6) << 20), __double2loint(tv));
 }
@@ -324,33 +329,34 @@ struct WarpCands {
   }
 };
 
-template <int KC, bool VEC2>
-__global__ void __launch_bounds__(topk::NT, 8)   // eight CTAs per SM (64 registers): one wave of rows
-block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
-                  int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
-  using namespace topk;
-  __shared__ double s_m[NW], s_r[NW], s_s[NW];
-  __shared__ double s_cx[NW * KC];
-  __shared__ int s_ci[NW * KC];
-  __shared__ double s_fx[KC], s_flp[KC];
-  __shared__ int s_fi[KC];
-  __shared__ double w_x[NW][CAP];
-  __shared__ int w_i[NW][CAP];
-  const int64_t row = blockIdx.x;
-  const double* x = logits + row * row_stride;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// Shared memory of one row's top-k: warp candidate buffers, the merge lists and the exp table.
+template <int KC>
+struct TopkSmem {
+  double r[topk::NW], sum[topk::NW];
+  double cx[topk::NW * KC];
+  int ci[topk::NW * KC];
+  double fx[KC], flp[KC];
+  int fi[KC];
+  double wx[topk::NW][topk::CAP];
+  int wi[topk::NW][topk::CAP];
+  double tab[64];
+};
 
-  __shared__ double s_tab[64];
-  exp2_table_init(s_tab);
-  __syncthreads();
-  WarpCands<KC> wc{w_x[warp], w_i[warp], 0, -INFINITY, -1, false};
-  double ref = -INFINITY, s = 0.0;
-  // Elements of one batch; every lane runs the same number of batches (elements past the row
-  // are -inf and invalid). The log-sum reference moves once per batch: when the batch max
-  // exceeds it by more than 256, so every exp argument is at most 256.
-  // (arrays of 8 with constant indices after unrolling; entries past nb are ignored; index(u) gives
-  // the element's index and is evaluated only when an element enters the candidate buffer)
-  auto batch = [&](const double (&v)[8], auto&& index, const bool (&ok)[8], int nb, bool all_ok) {
+// One thread's share of a row: its warp's candidate buffer and its lazily rescaled fp64 sum of
+// exp(x - ref). The reference moves once per batch of 8 elements: when the batch max exceeds it by
+// more than 256, so every exp argument is at most 256.
+template <int KC>
+struct TopkRow {
+  WarpCands<KC> wc;
+  double ref, s;
+  const double* tab;
+
+  // A batch of up to 8 elements (nb valid slots; ok[u] marks elements inside the row, ALL_OK that all
+  // are; elements past the row are -inf). Every lane of the warp calls it the same number of times.
+  // index(u) gives element u's index; it is evaluated only when an element enters the buffer.
+  template <bool ALL_OK, typename IndexF>
+  __device__ __forceinline__ void add8(const double (&v)[8], IndexF&& index, const bool (&ok)[8], int nb) {
+    constexpr bool all_ok = ALL_OK;
     double mv[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) mv[u] = (u < nb && (all_ok || ok[u])) ? v[u] : -INFINITY;
@@ -363,51 +369,130 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
     // nothing next to a sum that holds a term of 1
     double e[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) e[u] = u < nb ? exp_tab(fmax(v[u] - ref, -708.0), s_tab) : 0.0;
+    for (int u = 0; u < 8; ++u) e[u] = u < nb ? exp_tab(fmax(v[u] - ref, -708.0), tab) : 0.0;
     s += ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));   // a tree: short dependency chain
-    // candidates: one vote per batch; the per-element offers (a ballot each, in element order) run
-    // only when some lane holds an element that clears the threshold as it stands at the batch start
+    // candidates: one vote per batch on its max; the per-element offers (a ballot each, in element
+    // order) run only when some lane's batch max clears the threshold as it stands at the batch start
     // (the threshold only rises, so this admits a superset of what the offers take in)
-    bool any = false;
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      any |= u < nb && (all_ok || ok[u]) && (!wc.full || v[u] >= wc.tx);
-    if (__any_sync(0xffffffffu, any)) {
+    if (__any_sync(0xffffffffu, !wc.full || bm >= wc.tx)) {
 #pragma unroll
       for (int u = 0; u < 8; ++u)
         if (u < nb) wc.offer(v[u], index(u), all_ok || ok[u]);
     }
-  };
+  }
+};
+
+// After the row: the CTA's KC best, M = the best, lse = log of the merged sums, lp = (x - M) - lse in
+// the reference's order, sorted by (lp desc, index asc); a tie at the k-th / KC-th lp hands the row
+// to block_topk_exact_kernel (top_idx[row][0] = -1).
+template <int KC>
+__device__ __forceinline__ void topk_finish(TopkRow<KC>& rw, TopkSmem<KC>& sm, int64_t V, int k, int64_t row,
+                                            int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
+  using namespace topk;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  rw.wc.cut();   // the warp's KC best, in order
+  double ref = rw.ref, s = rw.s;
+  // (reference, sum): warp, then CTA
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const double orf = __shfl_xor_sync(0xffffffffu, ref, off);
+    const double os = __shfl_xor_sync(0xffffffffu, s, off);
+    const double nr = fmax(ref, orf);
+    if (nr != -INFINITY) {
+      s = (ref == -INFINITY ? 0.0 : s * exp_fast(ref - nr)) + (orf == -INFINITY ? 0.0 : os * exp_fast(orf - nr));
+    }
+    ref = nr;
+  }
+  if (lane == 0) { sm.r[warp] = ref; sm.sum[warp] = s; }
+  for (int c = lane; c < KC; c += 32) {
+    sm.cx[warp * KC + c] = c < rw.wc.n ? rw.wc.x[c] : -INFINITY;
+    sm.ci[warp * KC + c] = c < rw.wc.n ? rw.wc.i[c] : -1;
+  }
+  merge_warp_lists<KC>(sm.cx, sm.ci, sm.fx, sm.fi);
+
+  if (tid == 0) {
+    const double M = sm.fi[0] >= 0 ? sm.fx[0] : -INFINITY;   // the row max is the best candidate
+    double S = 0.0;
+    for (int w = 0; w < NW; ++w)
+      if (sm.r[w] != -INFINITY) S += sm.sum[w] * exp_fast(sm.r[w] - M);
+    const double lse = log(S);
+    int n = 0;
+    for (int c = 0; c < KC; ++c) {
+      if (sm.fi[c] < 0) break;
+      sm.flp[c] = (sm.fx[c] - M) - lse;
+      ++n;
+    }
+    // stable insertion sort by (lp desc, index asc)
+    for (int a = 1; a < n; ++a) {
+      const double lv = sm.flp[a];
+      const int iv = sm.fi[a];
+      int c = a - 1;
+      while (c >= 0 && (sm.flp[c] < lv || (sm.flp[c] == lv && sm.fi[c] > iv))) {
+        sm.flp[c + 1] = sm.flp[c];
+        sm.fi[c + 1] = sm.fi[c];
+        --c;
+      }
+      sm.flp[c + 1] = lv;
+      sm.fi[c + 1] = iv;
+    }
+    const bool tie = V > KC && n == KC && sm.flp[k - 1] == sm.flp[KC - 1];
+    if (tie) {
+      top_idx[row * k] = -1;  // hands the row to block_topk_exact_kernel
+    } else {
+      for (int c = 0; c < k; ++c) {
+        top_idx[row * k + c] = c < n ? (int64_t)sm.fi[c] : (int64_t)0;
+        top_lp[row * k + c] = c < n ? sm.flp[c] : -INFINITY;
+      }
+    }
+  }
+}
+
+// Rows read with plain loads (any alignment): each thread loads 8 elements per batch.
+template <int KC, bool VEC2>
+__global__ void __launch_bounds__(topk::NT, 8)   // eight CTAs per SM (64 registers): one wave of rows
+block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stride, int k,
+                  int64_t* __restrict__ top_idx, double* __restrict__ top_lp) {
+  using namespace topk;
+  __shared__ TopkSmem<KC> sm;
+  const int64_t row = blockIdx.x;
+  const double* x = logits + row * row_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  exp2_table_init(sm.tab);
+  __syncthreads();
+  TopkRow<KC> rw{WarpCands<KC>{sm.wx[warp], sm.wi[warp], 0, -INFINITY, -1, false}, -INFINITY, 0.0, sm.tab};
   if (VEC2) {
     const double2* x2 = reinterpret_cast<const double2*>(x);
     const int64_t n2 = V >> 1;
     const int64_t n2_full = n2 - n2 % (4 * NT);   // batches every lane's loads stay inside
-    for (int64_t base = 0; base < n2; base += 4 * NT) {
-      const bool full_batch = base < n2_full;
-      double2 d[4];
-      bool okp[4];
+    int64_t base = 0;
+    for (; base < n2_full; base += 4 * NT) {
+      double v[8];
+      const bool ok[8] = {true, true, true, true, true, true, true, true};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int64_t ii = base + u * NT + tid;
-        okp[u] = full_batch || ii < n2;
-        d[u] = okp[u] ? __ldcs(x2 + ii) : make_double2(-INFINITY, -INFINITY);
+        const double2 d = __ldcs(x2 + base + u * NT + tid);
+        v[2 * u] = d.x; v[2 * u + 1] = d.y;
       }
+      rw.template add8<true>(v, [&](int u) { return (int)(2 * (base + (u >> 1) * NT + tid)) + (u & 1); }, ok, 8);
+    }
+    if (base < n2) {   // the last, partial batch
       double v[8];
       bool ok[8];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        v[2 * u] = d[u].x; v[2 * u + 1] = d[u].y;
-        ok[2 * u] = okp[u]; ok[2 * u + 1] = okp[u];
+        const int64_t ii = base + u * NT + tid;
+        const bool in = ii < n2;
+        const double2 d = in ? __ldcs(x2 + ii) : make_double2(-INFINITY, -INFINITY);
+        v[2 * u] = d.x; v[2 * u + 1] = d.y;
+        ok[2 * u] = in; ok[2 * u + 1] = in;
       }
-      auto index = [&](int u) { return (int)(2 * (base + (u >> 1) * NT + tid)) + (u & 1); };
-      batch(v, index, ok, 8, full_batch);
+      rw.template add8<false>(v, [&](int u) { return (int)(2 * (base + (u >> 1) * NT + tid)) + (u & 1); }, ok, 8);
     }
     if (V & 1) {   // the odd last element: lane 0 of warp 0, the warp calls together
       if (warp == 0) {
         double v[8] = {lane == 0 ? x[V - 1] : -INFINITY};
         bool ok[8] = {lane == 0};
-        auto index = [&](int) { return (int)(V - 1); };
-        batch(v, index, ok, 1, false);
+        rw.template add8<false>(v, [&](int) { return (int)(V - 1); }, ok, 1);
       }
     }
   } else {
@@ -420,65 +505,10 @@ block_topk_kernel(const double* __restrict__ logits, int64_t V, int64_t row_stri
         ok[u] = ii < V;
         v[u] = ok[u] ? x[ii] : -INFINITY;
       }
-      auto index = [&](int u) { return (int)(base + u * NT + tid); };
-      batch(v, index, ok, 8, false);
+      rw.template add8<false>(v, [&](int u) { return (int)(base + u * NT + tid); }, ok, 8);
     }
   }
-  wc.cut();   // the warp's KC best, in order
-
-  // (reference, sum): warp, then CTA
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    const double orf = __shfl_xor_sync(0xffffffffu, ref, off);
-    const double os = __shfl_xor_sync(0xffffffffu, s, off);
-    const double nr = fmax(ref, orf);
-    if (nr != -INFINITY) {
-      s = (ref == -INFINITY ? 0.0 : s * exp_fast(ref - nr)) + (orf == -INFINITY ? 0.0 : os * exp_fast(orf - nr));
-    }
-    ref = nr;
-  }
-  if (lane == 0) { s_r[warp] = ref; s_s[warp] = s; }
-  for (int c = lane; c < KC; c += 32) {
-    s_cx[warp * KC + c] = c < wc.n ? wc.x[c] : -INFINITY;
-    s_ci[warp * KC + c] = c < wc.n ? wc.i[c] : -1;
-  }
-  merge_warp_lists<KC>(s_cx, s_ci, s_fx, s_fi);
-
-  if (tid == 0) {
-    const double M = s_fi[0] >= 0 ? s_fx[0] : -INFINITY;   // the row max is the best candidate
-    double S = 0.0;
-    for (int w = 0; w < NW; ++w)
-      if (s_r[w] != -INFINITY) S += s_s[w] * exp_fast(s_r[w] - M);
-    const double lse = log(S);
-    int n = 0;
-    for (int c = 0; c < KC; ++c) {
-      if (s_fi[c] < 0) break;
-      s_flp[c] = (s_fx[c] - M) - lse;
-      ++n;
-    }
-    // stable insertion sort by (lp desc, index asc)
-    for (int a = 1; a < n; ++a) {
-      const double lv = s_flp[a];
-      const int iv = s_fi[a];
-      int c = a - 1;
-      while (c >= 0 && (s_flp[c] < lv || (s_flp[c] == lv && s_fi[c] > iv))) {
-        s_flp[c + 1] = s_flp[c];
-        s_fi[c + 1] = s_fi[c];
-        --c;
-      }
-      s_flp[c + 1] = lv;
-      s_fi[c + 1] = iv;
-    }
-    const bool tie = V > KC && n == KC && s_flp[k - 1] == s_flp[KC - 1];
-    if (tie) {
-      top_idx[row * k] = -1;  // hands the row to block_topk_exact_kernel
-    } else {
-      for (int c = 0; c < k; ++c) {
-        top_idx[row * k + c] = c < n ? (int64_t)s_fi[c] : (int64_t)0;
-        top_lp[row * k + c] = c < n ? s_flp[c] : -INFINITY;
-      }
-    }
-  }
+  topk_finish<KC>(rw, sm, V, k, row, top_idx, top_lp);
 }
 
 // Exact path of rows block_topk_kernel flagged (top_idx[row][0] == -1): one
