@@ -31,7 +31,8 @@ EXPORTS = ("cast_strerror", "cast_version", "cast_device_error", "cast_tree_attn
            "cast_tree_attn_workspace_size", "cast_tree_attn_plan", "cast_block_topk", "cast_build_tree",
            "cast_tree_attn_fwd_noalloc", "cast_tree_attn_store_fwd", "cast_tree_attn_store_workspace_size",
            "cast_tree_walk_greedy", "cast_select_global_topk", "cast_append_store", "cast_gather_cache",
-           "cast_test_set_wait_limit_ns", "cast_tree_attn_workspace_size_kv", "cast_kv_ragged_gather")
+           "cast_test_set_wait_limit_ns", "cast_tree_attn_workspace_size_kv", "cast_kv_ragged_gather",
+           "cast_test_set_tc_kernel")
 CAST_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 
@@ -133,6 +134,8 @@ def lib():
                                     c_vp, c_int, c_vp]
     L.cast_test_set_wait_limit_ns.restype = None
     L.cast_test_set_wait_limit_ns.argtypes = [ctypes.c_uint64]
+    L.cast_test_set_tc_kernel.restype = None
+    L.cast_test_set_tc_kernel.argtypes = [c_int]
     _LIB = L
     return L
 

@@ -13,6 +13,7 @@
 #include "attn_simt.cuh"
 #include "attn_tc.cuh"
 #include "attn_tc3.cuh"
+#include "attn_pair.cuh"
 #include "tree_build.cuh"
 #include "verify_ops.cuh"
 
@@ -24,6 +25,9 @@ std::atomic<int> g_sm_count[kMaxDevices];
 // Limit of the tensor-core kernel's pipeline waits for the launches that follow
 // (cast_test_set_wait_limit_ns); the default is the library-wide wait limit.
 std::atomic<uint64_t> g_pipeline_wait_ns{tc::kWaitLimitNs};
+// 16-bit tensor-core kernel of the regular-layout launches that follow (cast_test_set_tc_kernel):
+// 1 = CTA pairs (attn_pair_kernel, the default), 0 = single CTAs (attn_tc_kernel).
+std::atomic<int> g_tc_kernel{1};
 
 int sm_count() {
   int dev = 0;
@@ -325,6 +329,41 @@ int launch_tc(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
   return launch_tc_maps<false>(p, pl, dtype, st, mq, mk, mv, mk, mv);
 }
 
+// CTA-pair kernel: a cluster of two CTAs per 256-row block; K tiles arrive in 64-key halves (one
+// per CTA of the pair), V tiles in 64-dim halves of all 128 keys.
+int launch_pair(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  const int G = p.G;
+  if (!make_map(&mq, p.q, dtype, p.total_q, p.H_q, p.sq_m, p.sq_h, G, tcp::BM / G) ||
+      !make_map(&mk, p.k, dtype, p.total_kv, p.H_kv, p.sk_m, p.sk_h, 1, tcp::BN / 2) ||
+      !make_map(&mv, p.v, dtype, p.total_kv, p.H_kv, p.sv_m, p.sv_h, 1, tcp::BN))
+    return CAST_ERR_LAUNCH;
+  p.n_split = pl.n_split;
+  p.chunk = pl.chunk;
+  p.m_tiles = pl.m_blocks;
+  p.W = pl.W;
+  constexpr size_t kMaxSmem = 227 * 1024 - 8 * 1024;   // the kernel's static shared memory takes the rest
+  const size_t smem = tcp::smem_bytes(tcp::NST, G, pl.W);
+  if (smem > kMaxSmem) return CAST_ERR_PACK;
+  dim3 grid(2 * pl.m_blocks, p.B * p.H_kv, pl.n_split);
+  auto go = [&](auto bf16_c, auto nst_c) {
+    auto kern = tcp::attn_pair_kernel<decltype(bf16_c)::value, decltype(nst_c)::value>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, tcp::NT, smem, st>>>(p, mq, mk, mv);
+  };
+  if (dtype == CAST_BF16) go(std::true_type{}, std::integral_constant<int, tcp::NST>{});
+  else go(std::false_type{}, std::integral_constant<int, tcp::NST>{});
+  if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  if (pl.n_split > 1) {
+    const long long warps = (long long)p.total_q * p.H_q;
+    const int blocks = (int)((warps * 32 + 255) / 256);
+    if (dtype == CAST_BF16) attn_combine_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(p);
+    else attn_combine_kernel<__half><<<blocks, 256, 0, st>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
+  }
+  return CAST_OK;
+}
+
 
 }  // namespace
 }  // namespace cast
@@ -416,6 +455,10 @@ int cast_version(void) { return 100; }
 
 void cast_test_set_wait_limit_ns(uint64_t ns) {
   g_pipeline_wait_ns.store(ns == 0 ? tc::kWaitLimitNs : ns, std::memory_order_relaxed);
+}
+
+void cast_test_set_tc_kernel(int kernel) {
+  g_tc_kernel.store(kernel == 0 ? 0 : 1, std::memory_order_relaxed);
 }
 
 int cast_device_error(cast_stream_t stream) {
@@ -548,7 +591,8 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
       p.ws_o = static_cast<float*>(workspace);
       p.ws_ml = p.ws_o + (size_t)tp.n_split * total_q * H_q * D;
     }
-    return launch_tc(p, tp, dtype, st);
+    const int sel = g_tc_kernel.load(std::memory_order_relaxed);
+    return sel ? launch_pair(p, tp, dtype, st) : launch_tc(p, tp, dtype, st);
   }
   const SimtPlan pl = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sms);
   if (pl.ws_bytes > 0) {
