@@ -591,8 +591,11 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
       p.ws_o = static_cast<float*>(workspace);
       p.ws_ml = p.ws_o + (size_t)tp.n_split * total_q * H_q * D;
     }
-    const int sel = g_tc_kernel.load(std::memory_order_relaxed);
-    return sel ? launch_pair(p, tp, dtype, st) : launch_tc(p, tp, dtype, st);
+    // CTA pairs only when the largest head group fills whole pairs (G * max_pack a multiple of 256
+    // rows): a pair whose second CTA has few or no rows streams every key tile on two SMs, where the
+    // single-CTA kernel runs a short group on one SM.
+    const bool pair = g_tc_kernel.load(std::memory_order_relaxed) != 0 && ((long long)p.G * max_pack) % 256 == 0;
+    return pair ? launch_pair(p, tp, dtype, st) : launch_tc(p, tp, dtype, st);
   }
   const SimtPlan pl = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sms);
   if (pl.ws_bytes > 0) {

@@ -109,9 +109,11 @@ void cast_test_set_wait_limit_ns(uint64_t ns);
  * Testing hook (no counterpart in the reference). Chooses the 16-bit
  * tensor-core attention kernel of the regular-layout cast_tree_attn_fwd calls
  * this process makes afterwards: 1 (default) = CTA pairs (tcgen05
- * cta_group::2, one 256-row block over the two SMs of a TPC), 0 = single CTAs
- * (two 128-row query tiles per SM, the kernel store mode always uses). Both
- * compute the same function; tests run both against the oracle.
+ * cta_group::2, one 256-row block over the two SMs of a TPC) whenever
+ * (H_q / H_kv) * max_pack is a multiple of 256, single CTAs otherwise; 0 =
+ * single CTAs always (two 128-row query tiles per SM, the kernel store mode
+ * always uses). Both compute the same function; tests run both against the
+ * oracle.
  */
 void cast_test_set_tc_kernel(int kernel);
 

@@ -1,10 +1,11 @@
 """Both 16-bit tensor-core attention kernels against the CPU oracle and each other (GPU).
 
-Regular-layout bf16/fp16 calls run the CTA-pair kernel by default (tcgen05 cta_group::2: a 256-row
-block over the two SMs of a TPC, three S buffers per SM); the single-CTA kernel (two 128-row query
-tiles per SM) serves store mode and stays selectable through cast_test_set_tc_kernel. Every shape
-here runs through both: one to many key tiles, S = 0, P = 1, ragged batches, G from 1 to 16, a
-260-row head group (a pair whose second CTA holds 4 rows), split keys, and 0-length-pack neighbours.
+Regular-layout bf16/fp16 calls whose largest head group fills whole 256-row pairs run the CTA-pair
+kernel (tcgen05 cta_group::2: a 256-row block over the two SMs of a TPC, three S buffers per SM);
+the others, and store mode, run the single-CTA kernel (two 128-row query tiles per SM). The test
+hook cast_test_set_tc_kernel(0) forces the single-CTA kernel; the cases below put each shape through
+both where the pair applies: one to many key tiles, S = 0, P = 1, ragged batches, G from 1 to 16,
+a 260-row head group, split keys. "pair" cases have G * max_pack a multiple of 256.
 """
 import numpy as np
 import pytest
@@ -18,6 +19,12 @@ from oracle import tree as otree
 pytestmark = pytest.mark.gpu
 
 CASES = [
+    ("pair one tile", [100], [64], 32, 8),
+    ("pair ragged", [0, 129, 256, 1000, 4000, 37], [1, 64, 128, 127, 65, 128], 32, 8),
+    ("pair P=1 neighbour", [700, 300], [1, 128], 32, 8),
+    ("pair G=1", [500, 300], [100, 256], 8, 8),
+    ("pair G=16", [900, 64], [64, 16], 128, 8),
+    ("pair split keys", [20000, 15000], [128, 100], 32, 8),
     ("one tile", [100], [20], 32, 8),
     ("two tiles", [200], [30], 32, 8),
     ("many tiles", [3000], [64], 32, 8),
