@@ -226,8 +226,12 @@ def main():
     ap.add_argument("--dtype", choices=["bf16", "fp16", "fp32"], default="bf16")
     ap.add_argument("--graph", action="store_true",
                     help="also time the calls replayed from a CUDA graph (device time without host overhead)")
+    ap.add_argument("--kernel", choices=["auto", "single", "simt"], default="auto",
+                    help="16-bit attention kernel: the library's choice (CTA pairs where they apply), "
+                         "single-CTA tcgen05 always, or the CUDA-core kernel (to measure the dispatch)")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
+    _lib.lib().cast_test_set_tc_kernel({"auto": 1, "single": 0, "simt": -1}[args.kernel])
     if args.what == "vs_triton":
         vs_triton(args, dev)
         return
@@ -363,6 +367,11 @@ def main():
             rec["bound"] = bound
             rec["frac_of_burst_peak"] = round((rec["tflops"] / tf) if bound == "tensor" else (rec["gbs"] / hbm), 3)
         rec["peaks"] = src
+        if args.what == "attn":
+            kern, n_split, _ = cast_b200.attention_plan(q, k, v, out, w.B, lay["max_pack"], lay["max_kv"])
+            pair = kern == "tcgen05" and args.kernel == "auto" and (w.H_q // w.H_kv) * lay["max_pack"] % 256 == 0
+            rec["kernel"] = "tcgen05 CTA pairs" if pair else ("tcgen05 single CTAs" if kern == "tcgen05" else kern)
+            rec["key_splits"] = n_split
     if args.what in ("walk", "append"):
         acc = walk_out.accepted.cpu()
         rec["mean_accepted"] = round(float(acc.float().mean()), 2)

@@ -25,8 +25,9 @@ std::atomic<int> g_sm_count[kMaxDevices];
 // Limit of the tensor-core kernel's pipeline waits for the launches that follow
 // (cast_test_set_wait_limit_ns); the default is the library-wide wait limit.
 std::atomic<uint64_t> g_pipeline_wait_ns{tc::kWaitLimitNs};
-// 16-bit tensor-core kernel of the regular-layout launches that follow (cast_test_set_tc_kernel):
-// 1 = CTA pairs (attn_pair_kernel, the default), 0 = single CTAs (attn_tc_kernel).
+// 16-bit kernel of the regular-layout launches that follow (cast_test_set_tc_kernel): 1 = CTA pairs
+// (attn_pair_kernel) where they apply, the default; 0 = single CTAs (attn_tc_kernel); -1 = the
+// CUDA-core kernel (attn_simt_kernel), for measuring the dispatch.
 std::atomic<int> g_tc_kernel{1};
 
 int sm_count() {
@@ -458,7 +459,7 @@ void cast_test_set_wait_limit_ns(uint64_t ns) {
 }
 
 void cast_test_set_tc_kernel(int kernel) {
-  g_tc_kernel.store(kernel == 0 ? 0 : 1, std::memory_order_relaxed);
+  g_tc_kernel.store(kernel < 0 ? -1 : (kernel == 0 ? 0 : 1), std::memory_order_relaxed);
 }
 
 int cast_device_error(cast_stream_t stream) {
@@ -515,7 +516,7 @@ int cast_tree_attn_plan(int dtype, int B, int total_q, int H_q, int H_kv, int D,
     plan[2] = tp.n_split > 1 ? 3 : 2;
     return CAST_OK;
   }
-  if (tc_eligible(dtype, D, H_q / H_kv, strides, q, k, v, out)) {
+  if (tc_eligible(dtype, D, H_q / H_kv, strides, q, k, v, out) && g_tc_kernel.load(std::memory_order_relaxed) >= 0) {
     const TcPlan tp = plan_tc(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
     plan[0] = 1;
     plan[1] = tp.n_split;
@@ -584,7 +585,7 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
     }
     return launch_tc3(p, tp, lay, ws, plain_split_args(p, lay, ws), sms, st);
   }
-  if (tc_eligible(dtype, D, p.G, strides, q, k, v, out)) {
+  if (tc_eligible(dtype, D, p.G, strides, q, k, v, out) && g_tc_kernel.load(std::memory_order_relaxed) >= 0) {
     const TcPlan tp = plan_tc(B, total_q, H_q, H_kv, max_pack, max_kv, sms);
     if (tp.ws_bytes > 0) {
       if (!workspace || workspace_bytes < tp.ws_bytes || !aligned(workspace, 16)) return CAST_ERR_WORKSPACE;

@@ -112,7 +112,8 @@ void cast_test_set_wait_limit_ns(uint64_t ns);
  * cta_group::2, one 256-row block over the two SMs of a TPC) whenever
  * (H_q / H_kv) * max_pack is a multiple of 256, single CTAs otherwise; 0 =
  * single CTAs always (two 128-row query tiles per SM, the kernel store mode
- * always uses). Both compute the same function; tests run both against the
+ * always uses); -1 = the CUDA-core kernel for every dtype (to measure the
+ * dispatch). All compute the same function; tests run each against the
  * oracle.
  */
 void cast_test_set_tc_kernel(int kernel);
