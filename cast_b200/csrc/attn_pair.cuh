@@ -63,7 +63,7 @@ __host__ __device__ constexpr int smem_v(int nst) { return SMEM_K + nst * KH_BYT
 __host__ __device__ constexpr int smem_anc(int nst) { return smem_v(nst) + nst * VH_BYTES; }
 __host__ __device__ inline int anc_tokens(int G) { return BM / G + 2; }
 __host__ __device__ inline size_t smem_bytes(int nst, int G, int W) {
-  return 1024 + smem_anc(nst) + (size_t)anc_tokens(G) * W * sizeof(uint64_t);
+  return 1024 + smem_anc(nst) + (size_t)anc_tokens(G) * W * sizeof(uint64_t) + parent_stage_bytes(W);
 }
 
 struct Bars {
@@ -156,53 +156,69 @@ attn_pair_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, co
     tma_prefetch_desc(&tmV);
   }
   if (warp == 0) tmem_alloc_pair(smem_u32(&tmem_base_sh), 512);
-  // ancestor bitsets of this CTA's tokens (rows past the pack read the last token's)
+  // ancestor bitsets of this CTA's tokens (rows past the pack read the last token's); the pack's
+  // parents up to the last of them are staged for the walks
   const int i_lo = min(r_cta / G, m.P - 1);
   const int i_hi = min(m.P - 1, (r_cta + BM - 1) / G);
-  if (has_pack_tile) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc);
+  int* sPar = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(sAnc) + (size_t)anc_tokens(G) * p.W * sizeof(uint64_t));
+  const bool stage = has_pack_tile && p.anc_words == nullptr && p.W <= kStageParentMaxW;
+  if (stage)
+    for (int j = tid; j <= i_hi; j += NT) sPar[j] = p.parent[m.q0 + j];
   fence_before_sync();
-  cluster_sync();   // barriers initialised and tensor memory allocated in both CTAs
+  cluster_sync();   // barriers initialised and tensor memory allocated in both CTAs, parents staged
   fence_after_sync();
   const uint32_t tmem = tmem_base_sh;
+
+  // TMA producers: warp 0 loads Q and the K ring, warp 2 the V ring (a V slot frees only when its
+  // PV completes, two tiles after its QK). Every copy of the pair completes on the even CTA's
+  // barrier, which expects both CTAs' bytes.
+  const bool is_k = warp == 0;
+  uint64_t* full = is_k ? bars.k_full : bars.v_full;
+  uint64_t* empty = is_k ? bars.k_empty : bars.v_empty;
+  auto issue_tile = [&](int j) {
+    const int s = j % NST;
+    const int key0 = m.kv0 + k_begin + j * BN;
+    if (elect_one()) {
+      if (lead) mbar_expect_tx(smem_u32(&full[s]), 2 * (is_k ? KH_BYTES : VH_BYTES));
+      const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+      if (is_k) {
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d_pair(smem_u32(smem + SMEM_K + s * KH_BYTES + hf * K_PANEL), &tmK, hf * 64, h,
+                           key0 + (int)crank * (BN / 2), fb);
+      } else {
+        tma_load_3d_pair(smem_u32(smem + SMEM_V + s * VH_BYTES), &tmV, (int)crank * 64, h, key0, fb);
+      }
+    }
+    __syncwarp();
+  };
+  // Q and the first NST key tiles need no free slot: their copies go out before the bitsets are built.
+  const int n_early = min(NST, n_kt);
+  if (warp == 0 || warp == 2) {
+    if (is_k && elect_one()) {
+      if (lead) mbar_expect_tx(smem_u32(&bars.q_full), 2 * Q_BYTES);
+      const uint32_t qf = mapa_shared(smem_u32(&bars.q_full), 0);
+      const int tok = m.q0 + r_cta / G;
+      for (int hf = 0; hf < 2; ++hf)
+        tma_load_3d_pair(smem_u32(smem + SMEM_Q + hf * Q_PANEL), &tmQ, hf * 64, h * G, tok, qf);
+    }
+    __syncwarp();
+    for (int j = 0; j < n_early; ++j) issue_tile(j);
+  }
+  if (has_pack_tile) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc, stage ? sPar : nullptr);
+  __syncthreads();   // bitsets built
 
   if (warp < 4) {
     regs_dec<kRegsLow>();
     if (warp == 0 || warp == 2) {
-      // ---------------------------------------------------------------- TMA producers
-      // Warp 0 loads Q and the K ring, warp 2 the V ring (a V slot frees only when its PV completes,
-      // two tiles after its QK): in each ring slot j % NST is refilled once the MMAs of use j - NST
-      // completed.
-      const bool is_k = warp == 0;
-      uint64_t* full = is_k ? bars.k_full : bars.v_full;
-      uint64_t* empty = is_k ? bars.k_empty : bars.v_empty;
-      if (is_k && elect_one()) {
-        if (lead) mbar_expect_tx(smem_u32(&bars.q_full), 2 * Q_BYTES);
-        const uint32_t qf = mapa_shared(smem_u32(&bars.q_full), 0);
-        const int tok = m.q0 + r_cta / G;
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_3d_pair(smem_u32(smem + SMEM_Q + hf * Q_PANEL), &tmQ, hf * 64, h * G, tok, qf);
-      }
-      __syncwarp();
-      int issued = 0;
-      for (int j = 0; j < n_kt; ++j) {
+      // ---------------------------------------------------------------- TMA producers (continued)
+      // In each ring slot j % NST is refilled once the MMAs of use j - NST completed.
+      int issued = n_early;
+      for (int j = n_early; j < n_kt; ++j) {
         const int s = j % NST;
         const uint32_t use = (uint32_t)(j / NST);
-        const int key0 = m.kv0 + k_begin + j * BN;
-        if (j >= NST &&
-            !__all_sync(0xffffffffu, mbar_wait(smem_u32(&empty[s]), (use - 1) & 1, abort_flag, p.wait_ns)))
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&empty[s]), (use - 1) & 1, abort_flag, p.wait_ns)))
           break;
-        if (elect_one()) {
-          if (lead) mbar_expect_tx(smem_u32(&full[s]), 2 * (is_k ? KH_BYTES : VH_BYTES));
-          const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
-          if (is_k) {
-            for (int hf = 0; hf < 2; ++hf)
-              tma_load_3d_pair(smem_u32(smem + SMEM_K + s * KH_BYTES + hf * K_PANEL), &tmK, hf * 64, h,
-                               key0 + (int)crank * (BN / 2), fb);
-          } else {
-            tma_load_3d_pair(smem_u32(smem + SMEM_V + s * VH_BYTES), &tmV, (int)crank * 64, h, key0, fb);
-          }
-        }
-        __syncwarp();
+        issue_tile(j);
         issued = j + 1;
       }
       if (lead) {
@@ -300,26 +316,10 @@ attn_pair_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, co
       const uint32_t S_t = tmem + lane_off + bj * 128;
       const int n0 = k_begin + j * BN;
       const bool full = (n0 + BN <= m.S) && (n0 + BN <= k_end);
-      auto mask32 = [&](int nb) -> uint32_t {
-        uint32_t bits = 0;
-#pragma unroll 1
-        for (int i = 0; i < 32; ++i) {
-          const int n = nb + i;
-          bool ok_k = n < k_end;
-          if (ok_k && n >= m.S) {
-            const int jj = n - m.S;
-            ok_k = (anc[jj >> 6] >> (jj & 63)) & 1ull;
-          }
-          bits |= (ok_k ? 1u : 0u) << i;
-        }
-        return bits;
-      };
       uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
       if (!full) {
-        vis[0] = mask32(n0);
-        vis[1] = mask32(n0 + 32);
-        vis[2] = mask32(n0 + 64);
-        vis[3] = mask32(n0 + 96);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) vis[c4] = visible32(anc, p.W, n0 + 32 * c4, m.S, k_end);
       }
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) tmem_ld32(S_t + cc * 32, sv + cc * 32);

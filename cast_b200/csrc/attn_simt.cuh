@@ -67,11 +67,21 @@ template <int D> __host__ __device__ constexpr size_t smem_bytes(int W) {
 }
 }  // namespace simt
 
+// Largest bitset width (64-bit words per token) for which the tensor-core kernels stage the
+// pack's parents in shared memory before building the bitsets (W * 64 ints).
+constexpr int kStageParentMaxW = 8;
+__host__ __device__ inline size_t parent_stage_bytes(int W) {
+  return W <= kStageParentMaxW ? (size_t)W * 64 * sizeof(int) : 0;
+}
+
 // Builds the ancestor bitsets of pack tokens [i_lo, i_lo + nt) into s_anc
 // ([nt][W] words). One thread per token; each walks its own ancestor chain
-// (parent[j] < j, so the walk ends within j + 1 steps).
+// (parent[j] < j, so the walk ends within j + 1 steps), reading the parents
+// from `par` (the pack's parents staged in shared memory) when given, else
+// from global memory. Bits are gathered one word at a time (the chain only
+// descends) and each word is stored once.
 __device__ __forceinline__ void build_tile_bitsets(const AttnParams& p, const SeqMeta& m, int i_lo,
-                                                   int nt, uint64_t* s_anc) {
+                                                   int nt, uint64_t* s_anc, const int* par = nullptr) {
   const int W = p.W;
   const int wn = (m.P + 63) >> 6;
   for (int li = threadIdx.x; li < nt; li += blockDim.x) {
@@ -85,9 +95,16 @@ __device__ __forceinline__ void build_tile_bitsets(const AttnParams& p, const Se
     } else {
       int j = i;
       int guard = 0;
+      int cw = j >> 6;
+      uint64_t acc = 0ull;
       while (j >= 0 && guard <= i) {
-        row[j >> 6] |= 1ull << (j & 63);
-        const int pj = p.parent[m.q0 + j];
+        if ((j >> 6) != cw) {
+          row[cw] = acc;
+          acc = 0ull;
+          cw = j >> 6;
+        }
+        acc |= 1ull << (j & 63);
+        const int pj = par != nullptr ? par[j] : p.parent[m.q0 + j];
         if (pj >= j || pj < -1 || (j == 0 && pj != -1)) {
           report(CAST_DEV_BAD_PARENT);
           break;
@@ -95,8 +112,30 @@ __device__ __forceinline__ void build_tile_bitsets(const AttnParams& p, const Se
         j = pj;
         ++guard;
       }
+      row[cw] = acc;
     }
   }
+}
+
+// Visibility of keys [nb, nb + 32) for one query row, bit i for key nb + i: prefix keys (< S) are
+// visible, pack key S + j iff bit j of the row token's bitset `anc` (W words), and keys at or past
+// `klim` are not. A shifted window of the bitset words, so a masked tile costs a few instructions
+// per 32 keys.
+__device__ __forceinline__ uint32_t visible32(const uint64_t* anc, int W, int nb, int S, int klim) {
+  uint32_t bits;
+  const int rel = nb - S;   // pack index of key nb (negative inside the prefix)
+  if (rel >= 0) {
+    const int w = rel >> 6, sh = rel & 63;
+    const uint64_t lo = w < W ? anc[w] : 0ull;
+    const uint64_t hi = (sh != 0 && w + 1 < W) ? anc[w + 1] : 0ull;
+    bits = (uint32_t)(sh != 0 ? (lo >> sh) | (hi << (64 - sh)) : lo);
+  } else if (rel > -32) {
+    bits = ((uint32_t)anc[0] << -rel) | ((1u << -rel) - 1u);   // -rel prefix keys, then pack bits 0..
+  } else {
+    bits = ~0u;
+  }
+  const int lim = klim - nb;
+  return lim >= 32 ? bits : (lim <= 0 ? 0u : bits & ((1u << lim) - 1u));
 }
 
 template <typename T, int D>

@@ -60,7 +60,7 @@ constexpr int kMaxRankedSeqs = 1024;
 
 __host__ __device__ inline int anc_tokens(int G) { return QT * BM / G + 2; }
 __host__ __device__ inline size_t smem_bytes(int G, int W) {
-  return 1024 + SMEM_ANC + (size_t)anc_tokens(G) * W * sizeof(uint64_t);
+  return 1024 + SMEM_ANC + (size_t)anc_tokens(G) * W * sizeof(uint64_t) + parent_stage_bytes(W);
 }
 
 struct Bars {
@@ -233,7 +233,56 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   if (warp == 0) tmem_alloc(smem_u32(&tmem_base_sh), 512);
   const int i_lo = r_base / G;
   const int i_hi = min(m.P - 1, (r_base + QT * BM - 1) / G);
-  if (has_pack_tile) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc);
+  // the pack's parents up to the last token of the block, staged for the bitset walks
+  int* sPar = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(sAnc) + (size_t)anc_tokens(G) * p.W * sizeof(uint64_t));
+  const bool stage = has_pack_tile && p.anc_words == nullptr && p.W <= kStageParentMaxW;
+  if (stage)
+    for (int j = tid; j <= i_hi; j += NT) sPar[j] = p.parent[m.q0 + j];
+  __syncthreads();   // barriers initialised, parents staged
+
+  // TMA producers: warp 0 loads the Q tiles and the K ring, warp 2 the V ring (a K slot frees up
+  // after the second QK of its tile, a V slot only after the second PV, so one loop over both would
+  // hold every K copy back behind the previous V slot).
+  const bool is_k = warp == 0;
+  const uint32_t qf = smem_u32(&bars.q_full);
+  uint64_t* full = is_k ? bars.k_full : bars.v_full;
+  uint64_t* empty = is_k ? bars.k_empty : bars.v_empty;
+  const uint32_t ring = smem_u32(smem + (is_k ? SMEM_K : SMEM_V));
+  const CUtensorMap* m_reg = is_k ? &tmK : &tmV;
+  const CUtensorMap* m_pack = is_k ? &tmKp : &tmVp;
+  // one 128-key tile (two 64-column halves) into ring slot j % NST
+  auto issue_tile = [&](int j) {
+    if (elect_one()) {
+      const uint32_t dst = ring + (j % NST) * TILE_BYTES, bar = smem_u32(&full[j % NST]);
+      mbar_expect_tx(bar, TILE_BYTES);
+      for (int hf = 0; hf < 2; ++hf) {
+        if constexpr (STORE) {
+          const int t = t_begin + j;
+          if (t < nt_pre) tma_load_4d(dst + hf * HALF_BYTES, m_reg, hf * 64, t * BN, h, b, bar);
+          else tma_load_3d(dst + hf * HALF_BYTES, m_pack, hf * 64, h, m.q0 + (t - nt_pre) * BN, bar);
+        } else {
+          tma_load_3d(dst + hf * HALF_BYTES, m_reg, hf * 64, h, m.kv0 + k_begin + j * BN, bar);
+        }
+      }
+    }
+    __syncwarp();
+  };
+  // The Q tiles and the first NST key tiles need no free slot: their copies go out before the
+  // ancestor bitsets are built.
+  const int n_early = min(NST, n_kt);
+  if (warp == 0 || warp == 2) {
+    if (is_k && elect_one()) {
+      mbar_expect_tx(qf, n_qt * TILE_BYTES);
+      for (int q = 0; q < n_qt; ++q) {
+        const int tok = m.q0 + (r_base + q * BM) / G;
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d(smem_u32(smem + SMEM_Q + q * TILE_BYTES + hf * HALF_BYTES), &tmQ, hf * 64, h * G, tok, qf);
+      }
+    }
+    __syncwarp();
+    for (int j = 0; j < n_early; ++j) issue_tile(j);
+  }
+  if (has_pack_tile) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc, stage ? sPar : nullptr);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -244,48 +293,13 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   // counters, shared-memory addresses, descriptors) stay in uniform registers;
   // one elected lane issues each TMA copy / MMA / commit.
   if (warp == 0 || warp == 2) {
-    // ------------------------------------------------------------ TMA producers
-    // Warp 0 loads the Q tiles and the K ring, warp 2 the V ring: a K slot frees up after the
-    // second QK of its tile, a V slot only after the second PV, so one loop over both would hold
-    // every K copy back behind the previous V slot.
-    const bool is_k = warp == 0;
-    const uint32_t qf = smem_u32(&bars.q_full);
-    if (is_k && elect_one()) {
-      mbar_expect_tx(qf, n_qt * TILE_BYTES);
-      for (int q = 0; q < n_qt; ++q) {
-        const int tok = m.q0 + (r_base + q * BM) / G;
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_3d(smem_u32(smem + SMEM_Q + q * TILE_BYTES + hf * HALF_BYTES), &tmQ, hf * 64, h * G, tok, qf);
-      }
-    }
-    __syncwarp();
-    uint64_t* full = is_k ? bars.k_full : bars.v_full;
-    uint64_t* empty = is_k ? bars.k_empty : bars.v_empty;
-    const uint32_t ring = smem_u32(smem + (is_k ? SMEM_K : SMEM_V));
-    const CUtensorMap* m_reg = is_k ? &tmK : &tmV;
-    const CUtensorMap* m_pack = is_k ? &tmKp : &tmVp;
-    int issued = 0;   // tiles whose copies were issued
-    for (int j = 0; j < n_kt; ++j) {
+    // ------------------------------------------------------------ TMA producers (continued)
+    int issued = n_early;   // tiles whose copies were issued
+    for (int j = n_early; j < n_kt; ++j) {
       const int s = j % NST;
       const uint32_t use = (uint32_t)(j / NST);
-      const int row = m.kv0 + k_begin + j * BN;
-      if (j >= NST && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&empty[s]), (use - 1) & 1, abort_flag, p.wait_ns)))
-        break;
-      if (elect_one()) {
-        const uint32_t dst = ring + s * TILE_BYTES, bar = smem_u32(&full[s]);
-        mbar_expect_tx(bar, TILE_BYTES);
-        // one 128-key tile (two 64-column halves) into the ring slot
-        for (int hf = 0; hf < 2; ++hf) {
-          if constexpr (STORE) {
-            const int t = t_begin + j;
-            if (t < nt_pre) tma_load_4d(dst + hf * HALF_BYTES, m_reg, hf * 64, t * BN, h, b, bar);
-            else tma_load_3d(dst + hf * HALF_BYTES, m_pack, hf * 64, h, m.q0 + (t - nt_pre) * BN, bar);
-          } else {
-            tma_load_3d(dst + hf * HALF_BYTES, m_reg, hf * 64, h, row, bar);
-          }
-        }
-      }
-      __syncwarp();
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&empty[s]), (use - 1) & 1, abort_flag, p.wait_ns))) break;
+      issue_tile(j);
       issued = j + 1;
     }
     // let the last copies land before the CTA can exit (immediate on the normal path); only
@@ -465,26 +479,10 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
         tile_keys(dual ? 2 * j + q : j, n0, klim);
         const bool full = (n0 + BN <= m.S) && (n0 + BN <= klim);
         // visibility bits of the 128 keys (only tiles that reach the pack or the chunk end)
-        auto mask32 = [&](int nb) -> uint32_t {
-          uint32_t bits = 0;
-#pragma unroll 1
-          for (int i = 0; i < 32; ++i) {
-            const int n = nb + i;
-            bool ok_k = n < klim;
-            if (ok_k && n >= m.S) {
-              const int jj = n - m.S;
-              ok_k = (anc[jj >> 6] >> (jj & 63)) & 1ull;
-            }
-            bits |= (ok_k ? 1u : 0u) << i;
-          }
-          return bits;
-        };
         uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
         if (!full) {
-          vis[0] = mask32(n0);
-          vis[1] = mask32(n0 + 32);
-          vis[2] = mask32(n0 + 64);
-          vis[3] = mask32(n0 + 96);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) vis[c4] = visible32(anc, p.W, n0 + 32 * c4, m.S, klim);
         }
         // the whole 128-column row of S in one round trip
 #pragma unroll

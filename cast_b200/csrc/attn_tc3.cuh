@@ -42,7 +42,7 @@ constexpr float kRescaleLog2 = 8.0f;
 
 __host__ __device__ inline int anc_tokens(int G) { return BM / G + 2; }
 __host__ __device__ inline size_t smem_bytes(int G, int W) {
-  return 1024 + SMEM_ANC + (size_t)anc_tokens(G) * W * sizeof(uint64_t);
+  return 1024 + SMEM_ANC + (size_t)anc_tokens(G) * W * sizeof(uint64_t) + parent_stage_bytes(W);
 }
 
 // ---- split pass -----------------------------------------------------------------
@@ -270,7 +270,14 @@ attn_tc3_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQh, co
   if (warp == 0) tmem_alloc(smem_u32(&tmem_base_sh), 256);
   const int i_lo = r_base / G;
   const int i_hi = min(m.P - 1, (r_base + BM - 1) / G);
-  if (has_pack_tile) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc);
+  // the pack's parents up to the last token of the tile, staged for the bitset walks
+  int* sPar = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(sAnc) + (size_t)anc_tokens(G) * p.W * sizeof(uint64_t));
+  const bool stage = has_pack_tile && p.anc_words == nullptr && p.W <= kStageParentMaxW;
+  if (stage) {
+    for (int j = tid; j <= i_hi; j += NT) sPar[j] = p.parent[m.q0 + j];
+    __syncthreads();
+  }
+  if (has_pack_tile) build_tile_bitsets(p, m, i_lo, i_hi - i_lo + 1, sAnc, stage ? sPar : nullptr);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -404,26 +411,10 @@ attn_tc3_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQh, co
       fence_after_sync();
       const int n0 = k_begin + j * BN, klim = k_end;
       const bool full = (n0 + BN <= m.S) && (n0 + BN <= klim);
-      auto mask32 = [&](int nb) -> uint32_t {
-        uint32_t bits = 0;
-#pragma unroll 1
-        for (int i = 0; i < 32; ++i) {
-          const int n = nb + i;
-          bool vis = n < klim;
-          if (vis && n >= m.S) {
-            const int jj = n - m.S;
-            vis = (anc[jj >> 6] >> (jj & 63)) & 1ull;
-          }
-          bits |= (vis ? 1u : 0u) << i;
-        }
-        return bits;
-      };
       uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
       if (!full) {
-        vis[0] = mask32(n0);
-        vis[1] = mask32(n0 + 32);
-        vis[2] = mask32(n0 + 64);
-        vis[3] = mask32(n0 + 96);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) vis[c4] = visible32(anc, p.W, n0 + 32 * c4, m.S, klim);
       }
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) tmem_ld32(S_t + cc * 32, sv + cc * 32);
