@@ -46,15 +46,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
-// As mbar_try_wait, with the thread suspended at most about `hint_ns` while it waits.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+// Non-blocking test of the phase with the given parity (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "r"(bar), "r"(parity)
       : "memory");
   return done != 0;
 }
@@ -70,11 +70,12 @@ constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           uint64_t limit_ns = kWaitLimitNs) {
   if (limit_ns < kWaitLimitNs) {
-    // a shortened limit (tests): a plain try_wait may stay suspended until the phase completes,
-    // so suspend briefly and read the timer on every round
+    // a shortened limit (tests, drains after an abort): try_wait may keep the thread suspended
+    // until the phase completes, however long, so poll without suspending and read the timer on
+    // every round
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-      if (mbar_try_wait_hint(bar, parity, 32)) return true;
+      if (mbar_test_wait(bar, parity)) return true;
       if (abort != nullptr && *abort) return false;
       if (globaltimer_ns() - t0 > limit_ns) {
         if (abort != nullptr) *abort = 1;
