@@ -838,10 +838,19 @@ int cast_build_tree(const int64_t* top_idx, const double* top_lp, int B, int L, 
   if (B == 0) return CAST_OK;
   TreeArgs a{top_idx, top_lp, B, L, k_cols, k, budget, max_budget, token, depth, parent, score, count,
              cu_q, pack_parent, root_token, pack_token, seq_len, pack_pos};
-  const size_t smem = tree_smem_bytes(max_budget > 0 ? max_budget : 1, L, k);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // candidate sets of up to 256 entries live in registers; larger budgets keep them in shared memory
+  const int mb = max_budget > 0 ? max_budget : 1;
+  if (mb + 1 <= 256) {
+    const size_t smem = tree_reg_smem_bytes(mb, L, k);
+    auto kern = mb + 1 <= 128 ? build_tree_reg_kernel<4> : build_tree_reg_kernel<8>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<B, 32, smem, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
+  }
+  const size_t smem = tree_smem_bytes(mb, L, k);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(build_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   build_tree_kernel<<<B, 32, smem, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? CAST_OK : CAST_ERR_LAUNCH;
 }

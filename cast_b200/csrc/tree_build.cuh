@@ -779,4 +779,208 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
   }
 }
 
+
+// build_tree with the candidate set in registers: candidate c sits in lane c % 32, register slot
+// c / 32 (SLOTS slots per lane, so budget + 1 <= 32 * SLOTS). Each key carries its whole payload:
+// hi = the ordered pattern of neg, lo = depth << 46 | (parent + 1) << 14 | rank << 6 | j << 1 | z
+// (j = position in the parent's child order, z = neg is -0.0). Candidates never share (depth,
+// parent, rank), so the bits below rank never decide an order, and (hi, lo) compares exactly like
+// the reference's (neg, depth, parent, rank). A pop is a scan of the lane's slots, a warp arg-min
+// over 64 bits (a second one over lo only on a tie), and an in-register replacement: no
+// shared-memory round trip sits on the pop chain except the neg of the popped node's parent.
+__device__ __forceinline__ double key_to_neg(uint64_t hi, uint64_t lo) {
+  if (lo & 1ull) return -0.0;
+  const uint64_t u = (hi >> 63) ? (hi & 0x7fffffffffffffffull) : ~hi;
+  return __longlong_as_double((long long)u);
+}
+__device__ __forceinline__ uint64_t cand_lo(int d, int par, int r, int j, double neg) {
+  const bool z = (uint64_t)__double_as_longlong(neg) == 0x8000000000000000ull;
+  return ((uint64_t)d << 46) | ((uint64_t)(uint32_t)(par + 1) << 14) | ((uint64_t)r << 6) | ((uint64_t)j << 1) |
+         (z ? 1ull : 0ull);
+}
+// warp-wide minimum of a 64-bit value (every lane gets it)
+__device__ __forceinline__ uint64_t warp_min64(uint64_t x, bool& mine) {
+  const uint32_t m0 = __reduce_min_sync(0xffffffffu, (uint32_t)(x >> 32));
+  mine = (uint32_t)(x >> 32) == m0;
+  const uint32_t m1 = __reduce_min_sync(0xffffffffu, mine ? (uint32_t)x : 0xffffffffu);
+  mine = mine && (uint32_t)x == m1;
+  return ((uint64_t)m0 << 32) | m1;
+}
+
+// candidate index c := (h, l): lane c % 32, slot c / 32 (compile-time slot indices only)
+template <int SLOTS>
+__device__ __forceinline__ void cand_put(uint64_t (&ch)[SLOTS], uint64_t (&cl)[SLOTS], int lane, int c, uint64_t h,
+                                         uint64_t l) {
+  const bool here = lane == (c & 31);
+  const int cs = c >> 5;
+#pragma unroll
+  for (int s = 0; s < SLOTS; ++s) {
+    const bool w = here && s == cs;
+    ch[s] = w ? h : ch[s];
+    cl[s] = w ? l : cl[s];
+  }
+}
+
+template <int SLOTS>
+__global__ void __launch_bounds__(32) build_tree_reg_kernel(const TreeArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x;
+  const int k = a.k, L = a.L;
+  double* n_neg = reinterpret_cast<double*>(smem_raw);                                  // neg of popped nodes
+  double* s_lp = n_neg + a.max_budget;
+  int32_t* s_tok = reinterpret_cast<int32_t*>(s_lp + (size_t)L * k);                  // token of each (row, rank)
+  unsigned char* order = reinterpret_cast<unsigned char*>(s_tok + (size_t)L * k);    // [(1 + max_budget)][k], row 0 = root
+
+  int budget = a.budget[b];
+  if (budget > a.max_budget || budget < 0) {
+    if (lane == 0) { report(CAST_DEV_TREE_OVERFLOW); a.count[b] = 0; }
+    return;
+  }
+  const double* lp_g = a.top_lp + (size_t)b * L * a.k_cols;
+  const int64_t* idx_g = a.top_idx + (size_t)b * L * a.k_cols;
+  bool sorted_rows = true;
+  for (int e = lane; e < L * k; e += 32) {
+    const double v = lp_g[(e / k) * a.k_cols + (e % k)];
+    s_lp[e] = v;
+    s_tok[e] = (int32_t)idx_g[(e / k) * a.k_cols + (e % k)];
+    if (e % k != k - 1 && !(v >= lp_g[(e / k) * a.k_cols + (e % k) + 1])) sorted_rows = false;
+  }
+  sorted_rows = __all_sync(0xffffffffu, sorted_rows);
+  __syncwarp();
+  auto child_order = [&](int slot, bool root, double base, int d) {
+    if (sorted_rows) return;
+    uint64_t hi = ~0ull;
+    if (lane < k) hi = ordered_key(root ? -s_lp[lane] : base - s_lp[d * k + lane]);
+    int rank = 0;
+    for (int r2 = 0; r2 < k; ++r2) {
+      const uint64_t h2 = __shfl_sync(0xffffffffu, hi, r2);
+      if (lane < k && (h2 < hi || (h2 == hi && r2 < lane))) ++rank;
+    }
+    if (lane < k) order[(size_t)slot * k + rank] = (unsigned char)lane;
+    __syncwarp();
+  };
+  auto nth_child = [&](int slot, int j) -> int { return sorted_rows ? j : (int)order[(size_t)slot * k + j]; };
+
+  uint64_t ch[SLOTS], cl[SLOTS];
+#pragma unroll
+  for (int s = 0; s < SLOTS; ++s) ch[s] = cl[s] = ~0ull;
+  int ncand = 0;
+  if (budget > 0 && k > 0 && L > 0) {
+    child_order(0, true, 0.0, 0);
+    const int r = nth_child(0, 0);
+    const double neg = -s_lp[r];
+    const uint64_t h0 = ordered_key(neg), l0 = cand_lo(1, -1, r, 0, neg);
+    cand_put<SLOTS>(ch, cl, lane, 0, h0, l0);
+    ncand = 1;
+  }
+
+  int n = 0;
+  const int q0 = a.cu_q ? a.cu_q[b] : 0;
+  const int pos0 = (a.cu_q && a.pack_pos) ? a.seq_len[b] : 0;
+  bool pack_ok = true;
+  if (a.cu_q && lane == 0) {
+    pack_ok = q0 >= 0 && (long long)q0 + 1 + budget <= (long long)a.cu_q[b + 1];
+    if (!pack_ok) report(CAST_DEV_BAD_LAYOUT);
+  }
+  pack_ok = __shfl_sync(0xffffffffu, pack_ok ? 1 : 0, 0) != 0;
+
+  while (n < budget && ncand > 0) {
+    // this lane's least candidate (empty slots hold all ones), then the warp's
+    uint64_t bh = ch[0], bl = cl[0];
+#pragma unroll
+    for (int s = 1; s < SLOTS; ++s)
+      if (ch[s] < bh || (ch[s] == bh && cl[s] < bl)) { bh = ch[s]; bl = cl[s]; }
+    bool mine;
+    const uint64_t wh = warp_min64(bh, mine);
+    const unsigned tied = __ballot_sync(0xffffffffu, mine);
+    uint64_t wl;
+    if (__popc(tied) == 1) {
+      wl = __shfl_sync(0xffffffffu, bl, __ffs(tied) - 1);
+    } else {
+      bool m2;
+      wl = warp_min64(mine ? bl : ~0ull, m2);
+    }
+    const int d = (int)(wl >> 46);
+    const int par = (int)(uint32_t)((wl >> 14) & 0xffffffffull) - 1;
+    const int r = (int)((wl >> 6) & 0xff);
+    const int j = (int)((wl >> 1) & 31);
+    const double neg = key_to_neg(wh, wl);
+    const int me = n;
+    if (lane == 0) {
+      const int tok = s_tok[(size_t)(d - 1) * k + r];
+      const size_t o = (size_t)b * a.max_budget + me;
+      a.token[o] = tok;
+      a.depth[o] = d;
+      a.parent[o] = par;
+      a.score[o] = -neg;
+      n_neg[me] = neg;
+      if (a.cu_q && pack_ok) {
+        if (a.pack_parent) a.pack_parent[q0 + 1 + me] = par + 1;
+        if (a.pack_token) a.pack_token[q0 + 1 + me] = tok;
+        if (a.pack_pos) a.pack_pos[q0 + 1 + me] = pos0 + d;
+      }
+    }
+    if (j + 1 < k) {
+      // the popped candidate becomes its next sibling
+      const int r2 = nth_child(par + 1, j + 1);
+      const double sneg = (par < 0) ? -s_lp[r2] : n_neg[par] - s_lp[(size_t)(d - 1) * k + r2];
+      const uint64_t nh = ordered_key(sneg), nl = cand_lo(d, par, r2, j + 1, sneg);
+#pragma unroll
+      for (int s = 0; s < SLOTS; ++s) {
+        const bool w = ch[s] == wh && cl[s] == wl;
+        ch[s] = w ? nh : ch[s];
+        cl[s] = w ? nl : cl[s];
+      }
+    } else {
+      // no sibling left: the last candidate moves into the popped one's place
+      const int last = ncand - 1;
+      // (a shuffle per slot: a select over slots by a run-time index would put the slots in memory)
+      uint64_t lh = ~0ull, ll = ~0ull;
+#pragma unroll
+      for (int s = 0; s < SLOTS; ++s) {
+        if (s <= (ncand - 1) >> 5) {
+          const uint64_t th = __shfl_sync(0xffffffffu, ch[s], last & 31);
+          const uint64_t tl = __shfl_sync(0xffffffffu, cl[s], last & 31);
+          lh = s == (last >> 5) ? th : lh;
+          ll = s == (last >> 5) ? tl : ll;
+        }
+      }
+      const bool last_here = lane == (last & 31);
+#pragma unroll
+      for (int s = 0; s < SLOTS; ++s) {
+        const bool w = ch[s] == wh && cl[s] == wl;    // the popped candidate: takes the last one's key
+        const bool e = last_here && s == (last >> 5);  // the last candidate's place: emptied
+        ch[s] = e ? ~0ull : (w ? lh : ch[s]);
+        cl[s] = e ? ~0ull : (w ? ll : cl[s]);
+      }
+      --ncand;
+    }
+    __syncwarp();   // n_neg[me] (lane 0) before any lane reads it
+    if (d < L) {
+      child_order(me + 1, false, neg, d);
+      const int r2 = nth_child(me + 1, 0);
+      const double cneg = neg - s_lp[(size_t)d * k + r2];
+      const uint64_t hc = ordered_key(cneg), lc = cand_lo(d + 1, me, r2, 0, cneg);
+      cand_put<SLOTS>(ch, cl, lane, ncand, hc, lc);
+      ++ncand;
+    }
+    ++n;
+  }
+  if (lane == 0) {
+    a.count[b] = n;
+    if (a.cu_q && pack_ok) {
+      if (a.pack_parent) a.pack_parent[q0] = -1;
+      if (a.pack_token) a.pack_token[q0] = a.root_token[b];
+      if (a.pack_pos) a.pack_pos[q0] = pos0;
+    }
+  }
+}
+
+__host__ __device__ inline size_t tree_reg_smem_bytes(int max_budget, int L, int k) {
+  return (size_t)max_budget * sizeof(double) +                  // node neg
+         ((size_t)max_budget + 1) * k * sizeof(unsigned char) +  // child order per node (+root)
+         (size_t)L * k * sizeof(double) +                        // lp rows
+         (size_t)L * k * sizeof(int32_t) + 64;                   // token rows
+}
 }  // namespace cast
