@@ -68,10 +68,11 @@ def test_noalloc_matches_the_workspace_entry_point_twice(cuda):
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
-    # a long-context batch (8 sequences, 32768-token prefixes, 129-token packs)
-    # splits into partials larger than the fixed array: rejected before any launch
+    # 18 sequences of 8192-token prefixes and 128-token packs: 288 (sequence, KV head, row block)
+    # units, fewer than two per SM, so the launch splits the keys in two, and the fp32 partials
+    # (2 x 2304 rows x 32 heads x 130 floats, 76.7 MB) exceed the fixed array: rejected before any launch
     L = _lib.lib()
-    B, S, P, Hq, Hkv, D = 8, 32768, 129, 32, 8, 128
+    B, S, P, Hq, Hkv, D = 18, 8192, 128, 32, 8, 128
     i32 = lambda x: torch.tensor(x, dtype=torch.int32, device=cuda)
     q = torch.empty(B * P, Hq, D, dtype=torch.bfloat16, device=cuda)
     k = torch.empty(B * (S + P), Hkv, D, dtype=torch.bfloat16, device=cuda)
