@@ -207,8 +207,11 @@ class Step:
         self.ws = None
 
     def run(self, layers, ev=None):
-        """One verify round; ev: optional (start, end) events around the attention calls."""
+        """One verify round; ev: optional (start, end, tree start) events: the first two around the
+        attention calls, the third before the tree build."""
         cb = self.cb
+        if ev is not None and len(ev) > 2:
+            ev[2].record()
         cb.block_topk_device(self.logits, 8, self.idx, self.lp)
         trees = cb.build_trees(self.idx, self.lp, self.budget, 8, max_budget=N_NODES, cu_q=self.cu_q,
                                root_token=self.roots, seq_len=self.seq_len, total_q=self.lay["total_q"])
@@ -278,7 +281,7 @@ def run_cast(args):
     flops = call_flops * args.layers          # per step
 
     stream = torch.cuda.current_stream()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(local).__enter__()      # sampled over both timed regions below
     time.sleep(0.3)                            # nvidia-smi start-up
@@ -293,8 +296,8 @@ def run_cast(args):
     if world > 1:
         _dist().barrier()
     step_ms = t0.elapsed_time(t1) / args.steps
-    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in evs) / args.layers   # per call
-    tree_ms = step_ms - attn_ms * args.layers
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in evs) / args.layers   # per call
+    tree_ms = statistics.mean(t.elapsed_time(a) for a, _, t in evs)                  # block_topk + build_tree
 
     # e2e: the public API with host buffers, every step's copies inside the timed region. The
     # loop is pipelined the way a server runs it: two device input sets, the host-to-device
