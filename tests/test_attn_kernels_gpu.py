@@ -78,3 +78,30 @@ def test_pair_and_single_kernels_match_oracle(cuda, name, S, P, Hq, Hkv, dtype):
         err = (out - expect).abs().max().item()
         assert err < 2e-2, (kernel, err)
     assert (outs[1] - outs[0]).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("kernel", [1, 0])
+def test_bad_metadata_is_reported_by_both_kernels(cuda, kernel):
+    # pair-eligible shape (4 heads per KV head x 64-token packs = 256 rows): a parent that is not in
+    # pack order, then a pack longer than the max_pack the caller promised. Both are recorded in the
+    # device error word, nothing hangs or faults, and the next good call on the context is correct.
+    q, k, v, cu_q, cu_kv, S_, P_, par = _case([300, 700], [64, 64], 32, 8, torch.bfloat16, 21)
+    t = lambda a: torch.from_numpy(a).to(cuda)
+    qd, kd, vd = q.to(cuda), k.to(cuda), v.to(cuda)
+    L = _lib.lib()
+    try:
+        L.cast_test_set_tc_kernel(kernel)
+        bad = par.copy()
+        bad[cu_q[1] + 5] = 9                          # token 5 of the second pack: parent after itself
+        cast_b200.varlen_tree_attention(qd, kd, vd, t(cu_q), t(cu_kv), t(S_), t(P_), None, parent=t(bad))
+        assert _lib.device_error() == _lib.CAST_DEV_BAD_PARENT
+        cast_b200.varlen_tree_attention(qd, kd, vd, t(cu_q), t(cu_kv), t(S_), t(P_), None, parent=t(par),
+                                        max_pack=32, max_kv=int((S_ + P_).max()))
+        assert _lib.device_error() == _lib.CAST_DEV_BAD_LAYOUT
+        out = cast_b200.varlen_tree_attention(qd, kd, vd, t(cu_q), t(cu_kv), t(S_), t(P_), None, parent=t(par))
+        assert _lib.device_error() == 0
+    finally:
+        L.cast_test_set_tc_kernel(1)
+    words = [otree.ancestor_words(par[cu_q[b]:cu_q[b + 1]]) for b in range(2)]
+    expect = oattn.tree_attention(q.float(), k.float(), v.float(), cu_q, cu_kv, S_, P_, words)
+    assert (out.float().cpu() - expect).abs().max().item() < 2e-2
