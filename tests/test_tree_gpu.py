@@ -156,3 +156,33 @@ def test_host_argument_errors(cuda):
         cast_b200.block_topk_device(x, 6)          # k > V
     with pytest.raises(_lib.CastError):
         cast_b200.block_topk_device(x, 0)
+
+
+@pytest.mark.parametrize("budget, k", [(40, 8), (127, 8), (200, 6)])
+def test_tied_logits_pipeline_bit_exact_against_reference(cuda, budget, k):
+    # Tie-heavy logits whose log-softmax is exact in both implementations: each row has a single 0
+    # (the maximum) and every other logit an integer <= -1000, so every other exp underflows (numpy
+    # gives 0; the library's clamped argument adds under 2^-1021, nothing next to the 1), the sum is
+    # exactly 1 and lse exactly 0. Every log-prob is then an exact integer, shared by hundreds of
+    # tokens, and every path score an exact integer sum: equal scores everywhere, so the tree's order
+    # is decided by the (depth, parent, rank) tie rule alone. The whole pipeline from raw logits must
+    # match the reference's numpy top-k and heap, bit for bit.
+    rng = np.random.default_rng(900 + budget)
+    B, L, V = 3, 9, 700
+    x = -1000.0 - rng.integers(0, 4, size=(B, L, V)).astype(np.float64)
+    x[np.arange(B)[:, None], np.arange(L)[None, :], rng.integers(0, V, size=(B, L))] = 0.0
+    xd = torch.from_numpy(x).to(cuda)
+    idx, lp = cast_b200.block_topk_device(xd, k)
+    trees = cast_b200.build_trees(idx, lp, budget, k)
+    assert _lib.device_error() == 0
+    for b in range(B):
+        oi, ol = otree.block_topk(x[b], k)
+        assert np.array_equal(idx[b].cpu().numpy(), oi)
+        assert np.array_equal(lp[b].cpu().numpy(), ol)
+        ref = otree.build_tree(oi, ol, budget, k)
+        n = int(trees.count[b])
+        assert n == len(ref)
+        assert np.array_equal(trees.token[b, :n].cpu().numpy(), ref.token)
+        assert np.array_equal(trees.depth[b, :n].cpu().numpy(), ref.depth)
+        assert np.array_equal(trees.parent[b, :n].cpu().numpy(), ref.parent)
+        assert np.array_equal(trees.score[b, :n].cpu().numpy().view(np.int64), ref.score.view(np.int64))
