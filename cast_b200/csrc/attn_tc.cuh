@@ -55,8 +55,11 @@ constexpr float kRescaleLog2 = 8.0f;          // lazy O rescale threshold (facto
 // warpgroups take 200: 128 x 104 + 256 x 200 = 64512.
 constexpr int kRegsLow = 104, kRegsHigh = 200;
 // Largest batch whose sequences the CTAs rank by length (longest first); larger
-// batches run in sequence order. The keys take 4 bytes each of the K ring.
-constexpr int kMaxRankedSeqs = 1024;
+// batches run in sequence order. Every CTA ranks the whole batch (O(B^2 / threads)):
+// at 512 sequences that took ~5 us per CTA and the ranked order was slower overall
+// than sequence order (configuration 5, one GPU: 3.06 against 3.25 ms at N = 16,
+// 12.9-13.3 against 13.6-13.8 ms at N = 128). The keys take 4 bytes each of the K ring.
+constexpr int kMaxRankedSeqs = 128;
 
 __host__ __device__ inline int anc_tokens(int G) { return QT * BM / G + 2; }
 __host__ __device__ inline size_t smem_bytes(int G, int W) {

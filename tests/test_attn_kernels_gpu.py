@@ -5,7 +5,8 @@ kernel (tcgen05 cta_group::2: a 256-row block over the two SMs of a TPC, three S
 the others, and store mode, run the single-CTA kernel (two 128-row query tiles per SM). The test
 hook cast_test_set_tc_kernel(0) forces the single-CTA kernel; the cases below put each shape through
 both where the pair applies: one to many key tiles, S = 0, P = 1, ragged batches, G from 1 to 16,
-a 260-row head group, split keys. "pair" cases have G * max_pack a multiple of 256.
+a 260-row head group, split keys, and batches of more sequences than the kernels rank by length.
+"pair" cases have G * max_pack a multiple of 256.
 """
 import numpy as np
 import pytest
@@ -25,6 +26,9 @@ CASES = [
     ("pair G=1", [500, 300], [100, 256], 8, 8),
     ("pair G=16", [900, 64], [64, 16], 128, 8),
     ("pair split keys", [20000, 15000], [128, 100], 32, 8),
+    # more sequences than the kernels rank by length (they then run in sequence order)
+    ("pair 160 sequences", [int(x) for x in np.random.default_rng(3).integers(0, 400, 160)],
+     [64] + [int(x) for x in np.random.default_rng(4).integers(1, 65, 159)], 32, 8),
     ("one tile", [100], [20], 32, 8),
     ("two tiles", [200], [30], 32, 8),
     ("many tiles", [3000], [64], 32, 8),
@@ -37,6 +41,8 @@ CASES = [
     ("G=16", [900, 64], [70, 16], 128, 8),
     ("260 rows", [2000], [65], 32, 8),
     ("split keys", [20000, 15000], [128, 100], 32, 8),
+    ("160 sequences", [int(x) for x in np.random.default_rng(5).integers(0, 400, 160)],
+     [int(x) for x in np.random.default_rng(6).integers(1, 50, 160)], 32, 8),
 ]
 
 
