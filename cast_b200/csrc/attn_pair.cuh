@@ -145,7 +145,7 @@ attn_pair_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, co
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&bars.pv_done[i]), 1);
-      for (int w = 0; w < 4; ++w) mbar_init(smem_u32(&bars.m_ready[i][w]), 32);
+      for (int w = 0; w < 4; ++w) mbar_init(smem_u32(&bars.m_ready[i][w]), 1);   // one arrival per warp
     }
     mbar_init(smem_u32(&bars.o_full), 1);
     mbar_init(smem_u32(&bars.comb), 2 * BM);
@@ -345,7 +345,8 @@ attn_pair_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, co
       const bool grow = m_tile > m_prev + kRescaleLog2 || (m_prev == -INFINITY && m_tile != -INFINITY);
       const float m_new = grow ? m_tile : m_prev;
       m_sh[j & 1][t] = m_new;
-      mbar_arrive(smem_u32(&bars.m_ready[j & 1][warp & 3]));
+      __syncwarp();   // the warp's m_sh writes are ordered before its lane 0's (releasing) arrival
+      if (lane == 0) mbar_arrive(smem_u32(&bars.m_ready[j & 1][warp & 3]));
       const bool rescale = grow && m_prev != -INFINITY;
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
