@@ -50,6 +50,9 @@ struct AttnParams {
   uint64_t wait_ns;
   // fp32 split path: flags[0..2] != 0 when the bf16 low parts of q / k / v hold any non-zero value
   const int* split_flags;
+  // Single-CTA tensor-core kernel: 1 when the largest head group ends in a one-tile block (G * max_pack
+  // mod 256 in (0, 128]): the launch then runs every other row block first and the last blocks after.
+  int tail_last;
 };
 
 // Key tiles of one sequence: the whole range for the regular layout, the

@@ -150,9 +150,17 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   // row block), row blocks fastest (the blocks of one head share its K/V tiles through L2), and
   // the sequence of that rank is found by ranking every sequence by S + P (descending, lower
   // index first): the longest units start first and the last wave holds the shortest ones.
+  // When the largest head group ends in a one-tile block (tail_last), that last row block of every
+  // (sequence, KV head, key chunk) goes after all the others: it costs about half a two-tile block,
+  // and with it interleaved the last wave held long two-tile units.
   const int L = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-  const int mblk = L % gridDim.x;
-  int rest = L / gridDim.x;
+  const int nb_first = (p.tail_last && gridDim.x > 1) ? gridDim.x - 1 : gridDim.x;
+  const int n_first = nb_first * gridDim.y * gridDim.z;
+  const bool late = L >= n_first;
+  const int Lr = late ? L - n_first : L;
+  const int nb = late ? 1 : nb_first;
+  const int mblk = late ? gridDim.x - 1 : Lr % nb;
+  int rest = Lr / nb;
   const int split = rest % gridDim.z;
   rest /= gridDim.z;
   const int h = rest % p.H_kv;

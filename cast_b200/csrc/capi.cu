@@ -201,6 +201,10 @@ int launch_tc_maps(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st, 
   p.chunk = pl.chunk;
   p.m_tiles = pl.m_blocks;
   p.W = pl.W;
+  {
+    const long long last = ((long long)p.G * p.max_pack) % (tca::QT * tca::BM);
+    p.tail_last = (last > 0 && last <= tca::BM) ? 1 : 0;
+  }
   const size_t smem = tca::smem_bytes(p.G, pl.W);
   dim3 grid(pl.m_blocks, p.B * p.H_kv, pl.n_split);
   if (dtype == CAST_BF16) {
