@@ -122,6 +122,7 @@ attn_pair_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, co
   const int rows = G * m.P;
   const int r_pair = mblk * (2 * BM);
   if (r_pair >= rows) return;
+  if (p.pair_full_only && r_pair + 2 * BM > rows) return;   // a partial block: the single-CTA launch takes it
   const int nkeys = m.S + m.P;
   const int k_begin = split * p.chunk;
   if (k_begin >= nkeys) return;

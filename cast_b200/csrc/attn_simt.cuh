@@ -53,6 +53,10 @@ struct AttnParams {
   // Single-CTA tensor-core kernel: 1 when the largest head group ends in a one-tile block (G * max_pack
   // mod 256 in (0, 128]): the launch then runs every other row block first and the last blocks after.
   int tail_last;
+  // Row-block selection when one call runs on both tensor-core kernels: the CTA-pair kernel takes
+  // only full 256-row blocks (pair_full_only), the single-CTA kernel only each sequence's partial
+  // last block (tail_only; its grid then holds one row block per (sequence, KV head, key chunk)).
+  int pair_full_only, tail_only;
 };
 
 // Key tiles of one sequence: the whole range for the regular layout, the

@@ -159,7 +159,7 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   const bool late = L >= n_first;
   const int Lr = late ? L - n_first : L;
   const int nb = late ? 1 : nb_first;
-  const int mblk = late ? gridDim.x - 1 : Lr % nb;
+  int mblk = late ? gridDim.x - 1 : Lr % nb;
   int rest = Lr / nb;
   const int split = rest % gridDim.z;
   rest /= gridDim.z;
@@ -180,6 +180,10 @@ attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ, cons
   }
   const int G = p.G;
   const int rows = G * m.P;
+  if (p.tail_only) {   // only the sequence's partial last 256-row block (the CTA-pair launch runs the rest)
+    if (rows % (QT * BM) == 0) return;
+    mblk = rows / (QT * BM);
+  }
   const int r_base = mblk * (QT * BM);
   if (r_base >= rows) return;
   const int n_qt = (rows - r_base > BM) ? 2 : 1;

@@ -196,7 +196,8 @@ bool make_store_map(CUtensorMap* map, const void* base, int dtype, int batch, in
 
 template <bool STORE>
 int launch_tc_maps(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st, const CUtensorMap& mq,
-                   const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mkp, const CUtensorMap& mvp) {
+                   const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mkp, const CUtensorMap& mvp,
+                   bool combine = true) {
   p.n_split = pl.n_split;
   p.chunk = pl.chunk;
   p.m_tiles = pl.m_blocks;
@@ -206,7 +207,7 @@ int launch_tc_maps(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st, 
     p.tail_last = (last > 0 && last <= tca::BM) ? 1 : 0;
   }
   const size_t smem = tca::smem_bytes(p.G, pl.W);
-  dim3 grid(pl.m_blocks, p.B * p.H_kv, pl.n_split);
+  dim3 grid(p.tail_only ? 1 : pl.m_blocks, p.B * p.H_kv, pl.n_split);
   if (dtype == CAST_BF16) {
     cudaFuncSetAttribute(tca::attn_tc_kernel<true, STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     tca::attn_tc_kernel<true, STORE><<<grid, tca::NT, smem, st>>>(p, mq, mk, mv, mkp, mvp);
@@ -215,7 +216,7 @@ int launch_tc_maps(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st, 
     tca::attn_tc_kernel<false, STORE><<<grid, tca::NT, smem, st>>>(p, mq, mk, mv, mkp, mvp);
   }
   if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
-  if (pl.n_split > 1) {
+  if (combine && pl.n_split > 1) {
     const long long warps = (long long)p.total_q * p.H_q;
     const int blocks = (int)((warps * 32 + 255) / 256);
     if (dtype == CAST_BF16) attn_combine_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(p);
@@ -326,19 +327,24 @@ bool split3_strides_ok(const int64_t* st, const void* q, const void* k, const vo
   return aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(out, 16);
 }
 
-int launch_tc(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
+int launch_tc(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st, bool combine = true) {
   CUtensorMap mq, mk, mv;
   const int G = p.G;
   if (!make_map(&mq, p.q, dtype, p.total_q, p.H_q, p.sq_m, p.sq_h, G, tca::BM / G) ||
       !make_map(&mk, p.k, dtype, p.total_kv, p.H_kv, p.sk_m, p.sk_h, 1, tca::BN) ||
       !make_map(&mv, p.v, dtype, p.total_kv, p.H_kv, p.sv_m, p.sv_h, 1, tca::BN))
     return CAST_ERR_LAUNCH;
-  return launch_tc_maps<false>(p, pl, dtype, st, mq, mk, mv, mk, mv);
+  return launch_tc_maps<false>(p, pl, dtype, st, mq, mk, mv, mk, mv, combine);
 }
 
 // CTA-pair kernel: a cluster of two CTAs per 256-row block; K tiles arrive in 64-key halves (one
 // per CTA of the pair), V tiles in 64-dim halves of all 128 keys.
-int launch_pair(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
+bool pair_fits(int G, int W) {
+  constexpr size_t kMaxSmem = 227 * 1024 - 8 * 1024;   // the kernel's static shared memory takes the rest
+  return tcp::smem_bytes(tcp::NST, G, W) <= kMaxSmem;
+}
+
+int launch_pair(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st, bool combine = true) {
   CUtensorMap mq, mk, mv;
   const int G = p.G;
   if (!make_map(&mq, p.q, dtype, p.total_q, p.H_q, p.sq_m, p.sq_h, G, tcp::BM / G) ||
@@ -361,7 +367,7 @@ int launch_pair(AttnParams& p, const TcPlan& pl, int dtype, cudaStream_t st) {
   if (dtype == CAST_BF16) go(std::true_type{}, std::integral_constant<int, tcp::NST>{});
   else go(std::false_type{}, std::integral_constant<int, tcp::NST>{});
   if (cudaGetLastError() != cudaSuccess) return CAST_ERR_LAUNCH;
-  if (pl.n_split > 1) {
+  if (combine && pl.n_split > 1) {
     const long long warps = (long long)p.total_q * p.H_q;
     const int blocks = (int)((warps * 32 + 255) / 256);
     if (dtype == CAST_BF16) attn_combine_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(p);
@@ -598,11 +604,29 @@ int cast_tree_attn_fwd(const void* q, const void* k, const void* v, void* out, i
       p.ws_o = static_cast<float*>(workspace);
       p.ws_ml = p.ws_o + (size_t)tp.n_split * total_q * H_q * D;
     }
-    // CTA pairs only when the largest head group fills whole pairs (G * max_pack a multiple of 256
-    // rows): a pair whose second CTA has few or no rows streams every key tile on two SMs, where the
-    // single-CTA kernel runs a short group on one SM.
-    const bool pair = g_tc_kernel.load(std::memory_order_relaxed) != 0 && ((long long)p.G * max_pack) % 256 == 0;
-    return pair ? launch_pair(p, tp, dtype, st) : launch_tc(p, tp, dtype, st);
+    // CTA pairs run the head groups' full 256-row blocks; a pair whose second CTA has few or no rows
+    // would stream every key tile on two SMs, so partial blocks go to the single-CTA kernel. When the
+    // largest head group fills whole pairs (G * max_pack a multiple of 256 rows) the pair kernel runs
+    // everything (a shorter group's partial block included). When it is longer than one pair, ends in
+    // a one-tile block and the units are long (key chunks of 64 tiles or more), the pair launch takes
+    // the full blocks and a single-CTA launch the partial last blocks, then the combine (if the keys
+    // are split) runs over both: configuration 4 714 -> 689 us, configuration 5 at N = 64, 128, 256
+    // 3-4 % faster. With short units (configuration 2: 74 -> 104 us) or a two-tile last block
+    // (configuration 5 at N = 96: 3 % slower) the two launches' tails cost more than the pairs save.
+    const long long gmp = (long long)p.G * max_pack;
+    const long long last = gmp % (tca::QT * tca::BM);
+    const bool pairs_on = g_tc_kernel.load(std::memory_order_relaxed) != 0 && pair_fits(p.G, tp.W);
+    if (pairs_on && last == 0) return launch_pair(p, tp, dtype, st);
+    if (pairs_on && gmp > tca::QT * tca::BM && last <= tca::BM && tp.chunk >= 64 * tca::BN) {
+      AttnParams pp = p;
+      pp.pair_full_only = 1;
+      const int rc = launch_pair(pp, tp, dtype, st, false);
+      if (rc != CAST_OK) return rc;
+      AttnParams ps = p;
+      ps.tail_only = 1;
+      return launch_tc(ps, tp, dtype, st);
+    }
+    return launch_tc(p, tp, dtype, st);
   }
   const SimtPlan pl = plan_simt(B, total_q, H_q, H_kv, D, max_pack, max_kv, sms);
   if (pl.ws_bytes > 0) {

@@ -5,7 +5,8 @@ kernel (tcgen05 cta_group::2: a 256-row block over the two SMs of a TPC, three S
 the others, and store mode, run the single-CTA kernel (two 128-row query tiles per SM). The test
 hook cast_test_set_tc_kernel(0) forces the single-CTA kernel; the cases below put each shape through
 both where the pair applies: one to many key tiles, S = 0, P = 1, ragged batches, G from 1 to 16,
-a 260-row head group, split keys, and batches of more sequences than the kernels rank by length.
+a 260-row head group (and long ones split between a pair launch and a single-CTA launch), split
+keys, and batches of more sequences than the kernels rank by length.
 "pair" cases have G * max_pack a multiple of 256.
 """
 import numpy as np
@@ -40,6 +41,8 @@ CASES = [
     ("G=8", [500, 1300], [100, 33], 64, 8),
     ("G=16", [900, 64], [70, 16], 128, 8),
     ("260 rows", [2000], [65], 32, 8),
+    # long units ending in a one-tile block: full 256-row blocks on CTA pairs, the last blocks on single CTAs
+    ("mixed pair and tail launches", [8192 + 37 * i for i in range(20)], [65] * 19 + [40], 32, 8),
     ("split keys", [20000, 15000], [128, 100], 32, 8),
     ("160 sequences", [int(x) for x in np.random.default_rng(5).integers(0, 400, 160)],
      [int(x) for x in np.random.default_rng(6).integers(1, 50, 160)], 32, 8),
