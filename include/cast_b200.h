@@ -110,11 +110,13 @@ void cast_test_set_wait_limit_ns(uint64_t ns);
  * tensor-core attention kernel of the regular-layout cast_tree_attn_fwd calls
  * this process makes afterwards: 1 (default) = CTA pairs (tcgen05
  * cta_group::2, one 256-row block over the two SMs of a TPC) whenever
- * (H_q / H_kv) * max_pack is a multiple of 256, single CTAs otherwise; 0 =
- * single CTAs always (two 128-row query tiles per SM, the kernel store mode
- * always uses); -1 = the CUDA-core kernel for every dtype (to measure the
- * dispatch). All compute the same function; tests run each against the
- * oracle.
+ * (H_q / H_kv) * max_pack is a multiple of 256; pairs for the full 256-row
+ * blocks and single CTAs for the last blocks when it is larger than 256,
+ * ends in a one-tile block and the key chunks are long; single CTAs
+ * otherwise; 0 = single CTAs always (two 128-row query tiles per SM, the
+ * kernel store mode always uses); -1 = the CUDA-core kernel for every dtype
+ * (to measure the dispatch). All compute the same function; tests run each
+ * against the oracle.
  */
 void cast_test_set_tc_kernel(int kernel);
 
