@@ -369,8 +369,18 @@ def main():
         rec["peaks"] = src
         if args.what == "attn":
             kern, n_split, _ = cast_b200.attention_plan(q, k, v, out, w.B, lay["max_pack"], lay["max_kv"])
-            pair = kern == "tcgen05" and args.kernel == "auto" and (w.H_q // w.H_kv) * lay["max_pack"] % 256 == 0
-            rec["kernel"] = "tcgen05 CTA pairs" if pair else ("tcgen05 single CTAs" if kern == "tcgen05" else kern)
+            # the library's dispatch (capi.cu): pairs when the largest head group fills whole 256-row
+            # pairs; pairs for the full blocks and single CTAs for the last ones when it is longer than a
+            # pair, ends in a one-tile block and the key chunks hold 64 tiles or more; else single CTAs
+            gmp = (w.H_q // w.H_kv) * lay["max_pack"]
+            chunk_tiles = -(-lay["max_kv"] // n_split // 128)
+            auto = kern == "tcgen05" and args.kernel == "auto"
+            if auto and gmp % 256 == 0:
+                rec["kernel"] = "tcgen05 CTA pairs"
+            elif auto and gmp > 256 and gmp % 256 <= 128 and chunk_tiles >= 64:
+                rec["kernel"] = "tcgen05 CTA pairs (full blocks) + single CTAs (last blocks)"
+            else:
+                rec["kernel"] = "tcgen05 single CTAs" if kern == "tcgen05" else kern
             rec["key_splits"] = n_split
     if args.what in ("walk", "append"):
         acc = walk_out.accepted.cpu()
