@@ -186,3 +186,45 @@ def test_tied_logits_pipeline_bit_exact_against_reference(cuda, budget, k):
         assert np.array_equal(trees.depth[b, :n].cpu().numpy(), ref.depth)
         assert np.array_equal(trees.parent[b, :n].cpu().numpy(), ref.parent)
         assert np.array_equal(trees.score[b, :n].cpu().numpy().view(np.int64), ref.score.view(np.int64))
+
+
+@pytest.mark.parametrize("max_budget", [127, 255])
+@pytest.mark.parametrize("kind", ["flat", "unsorted", "peaked", "zero_top", "integer_ties", "positive", "one_row"])
+def test_build_tree_on_any_rows_bit_exact(cuda, kind, max_budget):
+    # build_tree on top-k arrays given directly (not produced by block_topk): rows in any column order,
+    # rows whose best lp is 0 or -0.0 (a chain of equal scores), integer lp (ties everywhere), positive
+    # lp (children better than their parents). Flat rows take many nodes per batched step, peaked and
+    # zero-top rows mostly single pops; every field must equal the reference heap's, score bits included.
+    rng = np.random.default_rng(sum(map(ord, kind)) + max_budget)
+    B, k = 6, 8
+    L = 1 if kind == "one_row" else 15
+    idx = rng.integers(0, 128256, size=(B, L, k)).astype(np.int64)
+    if kind in ("flat", "unsorted", "one_row"):
+        lp = -np.sort(rng.exponential(2.0, size=(B, L, k)), axis=-1) - rng.exponential(1.0, size=(B, L, 1))
+    elif kind == "peaked":
+        lp = -np.sort(rng.exponential(3.0, size=(B, L, k)), axis=-1)
+        lp[..., 0] = -rng.exponential(1e-4, size=(B, L))
+    elif kind == "zero_top":
+        lp = -np.sort(rng.exponential(2.0, size=(B, L, k)), axis=-1)
+        lp[..., 0] = np.where(rng.random((B, L)) < 0.5, 0.0, -0.0)
+    elif kind == "integer_ties":
+        lp = -np.sort(rng.integers(0, 3, size=(B, L, k)), axis=-1).astype(np.float64)
+    else:
+        lp = np.sort(rng.normal(0.0, 1.0, size=(B, L, k)), axis=-1)[..., ::-1].copy()
+    if kind == "unsorted":
+        for b in range(B):
+            perm = rng.permutation(k)
+            idx[b], lp[b] = idx[b][:, perm], lp[b][:, perm]
+    budgets = rng.integers(0, max_budget + 1, size=B).astype(np.int32)
+    budgets[0] = max_budget
+    trees = cast_b200.build_trees(torch.from_numpy(idx).to(cuda), torch.from_numpy(lp).to(cuda),
+                                  torch.from_numpy(budgets).to(cuda), k, max_budget=max_budget)
+    assert _lib.device_error() == 0
+    for b in range(B):
+        ref = otree.build_tree(idx[b], lp[b], int(budgets[b]), k)
+        n = int(trees.count[b])
+        assert n == len(ref)
+        assert np.array_equal(trees.token[b, :n].cpu().numpy(), ref.token)
+        assert np.array_equal(trees.depth[b, :n].cpu().numpy(), ref.depth)
+        assert np.array_equal(trees.parent[b, :n].cpu().numpy(), ref.parent)
+        assert np.array_equal(trees.score[b, :n].cpu().numpy().view(np.int64), ref.score.view(np.int64))
