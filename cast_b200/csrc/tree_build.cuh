@@ -830,7 +830,8 @@ __global__ void __launch_bounds__(32) build_tree_reg_kernel(const TreeArgs a) {
   double* n_neg = reinterpret_cast<double*>(smem_raw);                                  // neg of popped nodes
   double* s_lp = n_neg + a.max_budget;
   int32_t* s_tok = reinterpret_cast<int32_t*>(s_lp + (size_t)L * k);                  // token of each (row, rank)
-  unsigned char* order = reinterpret_cast<unsigned char*>(s_tok + (size_t)L * k);    // [(1 + max_budget)][k], row 0 = root
+  int32_t* n_info = s_tok + (size_t)L * k;                     // popped node: (parent + 1) | depth << 16 | rank << 24
+  unsigned char* order = reinterpret_cast<unsigned char*>(n_info + a.max_budget);    // [(1 + max_budget)][k], row 0 = root
 
   int budget = a.budget[b];
   if (budget > a.max_budget || budget < 0) {
@@ -886,20 +887,24 @@ __global__ void __launch_bounds__(32) build_tree_reg_kernel(const TreeArgs a) {
   pack_ok = __shfl_sync(0xffffffffu, pack_ok ? 1 : 0, 0) != 0;
 
   while (n < budget && ncand > 0) {
-    // this lane's least candidate (empty slots hold all ones), then the warp's
+    // this lane's least candidate (empty slots hold all ones) and its slot, then the warp's
     uint64_t bh = ch[0], bl = cl[0];
+    int bs = 0;
 #pragma unroll
     for (int s = 1; s < SLOTS; ++s)
-      if (ch[s] < bh || (ch[s] == bh && cl[s] < bl)) { bh = ch[s]; bl = cl[s]; }
+      if (ch[s] < bh || (ch[s] == bh && cl[s] < bl)) { bh = ch[s]; bl = cl[s]; bs = s; }
     bool mine;
     const uint64_t wh = warp_min64(bh, mine);
     const unsigned tied = __ballot_sync(0xffffffffu, mine);
     uint64_t wl;
+    bool win;   // this lane holds the popped candidate, in slot bs (keys are unique)
     if (__popc(tied) == 1) {
       wl = __shfl_sync(0xffffffffu, bl, __ffs(tied) - 1);
+      win = mine;
     } else {
       bool m2;
       wl = warp_min64(mine ? bl : ~0ull, m2);
+      win = mine && m2;
     }
     const int d = (int)(wl >> 46);
     const int par = (int)(uint32_t)((wl >> 14) & 0xffffffffull) - 1;
@@ -907,19 +912,9 @@ __global__ void __launch_bounds__(32) build_tree_reg_kernel(const TreeArgs a) {
     const int j = (int)((wl >> 1) & 31);
     const double neg = key_to_neg(wh, wl);
     const int me = n;
-    if (lane == 0) {
-      const int tok = s_tok[(size_t)(d - 1) * k + r];
-      const size_t o = (size_t)b * a.max_budget + me;
-      a.token[o] = tok;
-      a.depth[o] = d;
-      a.parent[o] = par;
-      a.score[o] = -neg;
+    if (lane == 0) {   // the outputs are written after the loop, all lanes together
       n_neg[me] = neg;
-      if (a.cu_q && pack_ok) {
-        if (a.pack_parent) a.pack_parent[q0 + 1 + me] = par + 1;
-        if (a.pack_token) a.pack_token[q0 + 1 + me] = tok;
-        if (a.pack_pos) a.pack_pos[q0 + 1 + me] = pos0 + d;
-      }
+      n_info[me] = (par + 1) | (d << 16) | (r << 24);
     }
     if (j + 1 < k) {
       // the popped candidate becomes its next sibling
@@ -928,7 +923,7 @@ __global__ void __launch_bounds__(32) build_tree_reg_kernel(const TreeArgs a) {
       const uint64_t nh = ordered_key(sneg), nl = cand_lo(d, par, r2, j + 1, sneg);
 #pragma unroll
       for (int s = 0; s < SLOTS; ++s) {
-        const bool w = ch[s] == wh && cl[s] == wl;
+        const bool w = win && s == bs;
         ch[s] = w ? nh : ch[s];
         cl[s] = w ? nl : cl[s];
       }
@@ -949,7 +944,7 @@ __global__ void __launch_bounds__(32) build_tree_reg_kernel(const TreeArgs a) {
       const bool last_here = lane == (last & 31);
 #pragma unroll
       for (int s = 0; s < SLOTS; ++s) {
-        const bool w = ch[s] == wh && cl[s] == wl;    // the popped candidate: takes the last one's key
+        const bool w = win && s == bs;                 // the popped candidate: takes the last one's key
         const bool e = last_here && s == (last >> 5);  // the last candidate's place: emptied
         ch[s] = e ? ~0ull : (w ? lh : ch[s]);
         cl[s] = e ? ~0ull : (w ? ll : cl[s]);
@@ -967,6 +962,22 @@ __global__ void __launch_bounds__(32) build_tree_reg_kernel(const TreeArgs a) {
     }
     ++n;
   }
+  __syncwarp();
+  for (int me = lane; me < n; me += 32) {
+    const int info = n_info[me];
+    const int par = (info & 0xffff) - 1, d = (info >> 16) & 0xff, r = info >> 24;
+    const int tok = s_tok[(size_t)(d - 1) * k + r];
+    const size_t o = (size_t)b * a.max_budget + me;
+    a.token[o] = tok;
+    a.depth[o] = d;
+    a.parent[o] = par;
+    a.score[o] = -n_neg[me];
+    if (a.cu_q && pack_ok) {
+      if (a.pack_parent) a.pack_parent[q0 + 1 + me] = par + 1;
+      if (a.pack_token) a.pack_token[q0 + 1 + me] = tok;
+      if (a.pack_pos) a.pack_pos[q0 + 1 + me] = pos0 + d;
+    }
+  }
   if (lane == 0) {
     a.count[b] = n;
     if (a.cu_q && pack_ok) {
@@ -978,9 +989,9 @@ __global__ void __launch_bounds__(32) build_tree_reg_kernel(const TreeArgs a) {
 }
 
 __host__ __device__ inline size_t tree_reg_smem_bytes(int max_budget, int L, int k) {
-  return (size_t)max_budget * sizeof(double) +                  // node neg
-         ((size_t)max_budget + 1) * k * sizeof(unsigned char) +  // child order per node (+root)
-         (size_t)L * k * sizeof(double) +                        // lp rows
-         (size_t)L * k * sizeof(int32_t) + 64;                   // token rows
+  return (size_t)max_budget * (sizeof(double) + sizeof(int32_t)) +  // node neg and (parent, depth, rank)
+         ((size_t)max_budget + 1) * k * sizeof(unsigned char) +      // child order per node (+root)
+         (size_t)L * k * sizeof(double) +                            // lp rows
+         (size_t)L * k * sizeof(int32_t) + 64;                       // token rows
 }
 }  // namespace cast
