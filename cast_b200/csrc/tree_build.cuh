@@ -612,7 +612,7 @@ struct TreeArgs {
 __host__ __device__ inline size_t tree_smem_bytes(int max_budget, int L, int k) {
   const size_t nc = (size_t)max_budget + 1;
   return nc * (2 * sizeof(uint64_t) + sizeof(double) + 4 * sizeof(int)) +  // candidates
-         (size_t)max_budget * sizeof(double) +                            // node neg
+         (size_t)max_budget * (sizeof(double) + sizeof(int32_t)) +        // node neg and (parent, depth, rank)
          ((size_t)max_budget + 1) * k * sizeof(unsigned char) +            // child order per node (+root)
          (size_t)L * k * sizeof(double) +                                  // lp rows
          (size_t)L * k * sizeof(int32_t) + 64;                             // token rows
@@ -651,7 +651,8 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
   double* n_neg = reinterpret_cast<double*>(c_r + nc_max);
   double* s_lp = n_neg + a.max_budget;
   int32_t* s_tok = reinterpret_cast<int32_t*>(s_lp + (size_t)L * k);                // token of each (row, rank)
-  unsigned char* order = reinterpret_cast<unsigned char*>(s_tok + (size_t)L * k);  // [(1 + max_budget)][k], row 0 = root
+  int32_t* n_info = s_tok + (size_t)L * k;                     // popped node: (parent + 1) | depth << 16 | rank << 24
+  unsigned char* order = reinterpret_cast<unsigned char*>(n_info + a.max_budget);  // [(1 + max_budget)][k], row 0 = root
 
   int budget = a.budget[b];
   if (budget > a.max_budget || budget < 0) {
@@ -726,19 +727,9 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
     const int par = c_par[slot], j = c_j[slot], d = c_d[slot], r = c_r[slot];
     const int me = n;
     __syncwarp();  // every lane has read the slot before lane 0 rewrites it
-    if (lane == 0) {
-      const int tok = s_tok[(size_t)(d - 1) * k + r];
-      const size_t o = (size_t)b * a.max_budget + me;
-      a.token[o] = tok;
-      a.depth[o] = d;
-      a.parent[o] = par;
-      a.score[o] = -neg;
+    if (lane == 0) {   // the outputs are written after the loop, all lanes together
       n_neg[me] = neg;
-      if (a.cu_q && pack_ok) {
-        if (a.pack_parent) a.pack_parent[q0 + 1 + me] = par + 1;
-        if (a.pack_token) a.pack_token[q0 + 1 + me] = tok;
-        if (a.pack_pos) a.pack_pos[q0 + 1 + me] = pos0 + d;
-      }
+      n_info[me] = (par + 1) | (d << 16) | (r << 24);
       // the popped slot takes the next sibling, or the last candidate
       if (j + 1 < k) {
         const int r2 = nth_child(par + 1, j + 1);
@@ -768,6 +759,21 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
     }
     ++n;
     __syncwarp();
+  }
+  for (int me = lane; me < n; me += 32) {
+    const int info = n_info[me];
+    const int par = (info & 0xffff) - 1, d = (info >> 16) & 0xff, r = info >> 24;
+    const int tok = s_tok[(size_t)(d - 1) * k + r];
+    const size_t o = (size_t)b * a.max_budget + me;
+    a.token[o] = tok;
+    a.depth[o] = d;
+    a.parent[o] = par;
+    a.score[o] = -n_neg[me];
+    if (a.cu_q && pack_ok) {
+      if (a.pack_parent) a.pack_parent[q0 + 1 + me] = par + 1;
+      if (a.pack_token) a.pack_token[q0 + 1 + me] = tok;
+      if (a.pack_pos) a.pack_pos[q0 + 1 + me] = pos0 + d;
+    }
   }
   if (lane == 0) {
     a.count[b] = n;
