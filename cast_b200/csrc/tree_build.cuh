@@ -899,18 +899,28 @@ __global__ void __launch_bounds__(32) build_tree_reg_kernel(const TreeArgs a) {
 #pragma unroll
     for (int s = 1; s < SLOTS; ++s)
       if (ch[s] < bh || (ch[s] == bh && cl[s] < bl)) { bh = ch[s]; bl = cl[s]; bs = s; }
-    bool mine;
-    const uint64_t wh = warp_min64(bh, mine);
-    const unsigned tied = __ballot_sync(0xffffffffu, mine);
-    uint64_t wl;
+    // usually one lane alone holds the least upper word of hi: its candidate is the minimum
+    const uint32_t top = (uint32_t)(bh >> 32);
+    const unsigned first = __ballot_sync(0xffffffffu, top == __reduce_min_sync(0xffffffffu, top));
+    uint64_t wh, wl;
     bool win;   // this lane holds the popped candidate, in slot bs (keys are unique)
-    if (__popc(tied) == 1) {
-      wl = __shfl_sync(0xffffffffu, bl, __ffs(tied) - 1);
-      win = mine;
+    if (__popc(first) == 1) {
+      const int src = __ffs(first) - 1;
+      wh = __shfl_sync(0xffffffffu, bh, src);
+      wl = __shfl_sync(0xffffffffu, bl, src);
+      win = lane == src;
     } else {
-      bool m2;
-      wl = warp_min64(mine ? bl : ~0ull, m2);
-      win = mine && m2;
+      bool mine;
+      wh = warp_min64(bh, mine);
+      const unsigned tied = __ballot_sync(0xffffffffu, mine);
+      if (__popc(tied) == 1) {
+        wl = __shfl_sync(0xffffffffu, bl, __ffs(tied) - 1);
+        win = mine;
+      } else {
+        bool m2;
+        wl = warp_min64(mine ? bl : ~0ull, m2);
+        win = mine && m2;
+      }
     }
     const int d = (int)(wl >> 46);
     const int par = (int)(uint32_t)((wl >> 14) & 0xffffffffull) - 1;
