@@ -619,16 +619,25 @@ __host__ __device__ inline size_t tree_smem_bytes(int max_budget, int L, int k) 
 }
 
 // Warp-wide arg-min of a 128-bit key (hi, lo); every lane returns the winner's
-// slot (-1 if no lane has one). Four 32-bit redux.sync rounds, most
-// significant word first, then the one lane left holding the minimum.
+// slot (-1 if no lane has one). Up to four 32-bit redux.sync rounds, most
+// significant word first (one when a single lane holds the least first word),
+// then the one lane left holding the minimum.
 __device__ __forceinline__ int warp_argmin128(uint64_t hi, uint64_t lo, int slot) {
   unsigned live = 0xffffffffu;
   bool mine = slot >= 0;
-  const uint32_t w[4] = {(uint32_t)(hi >> 32), (uint32_t)hi, (uint32_t)(lo >> 32), (uint32_t)lo};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t m = __reduce_min_sync(0xffffffffu, mine ? w[i] : 0xffffffffu);
-    mine = mine && w[i] == m;
+  // every lane takes part in each reduction (computed before it is compared)
+  const uint32_t w0 = (uint32_t)(hi >> 32);
+  const uint32_t m0 = __reduce_min_sync(0xffffffffu, mine ? w0 : 0xffffffffu);
+  mine = mine && w0 == m0;
+  // usually one lane is left after the first word: the other words cannot change the winner
+  if (__popc(__ballot_sync(0xffffffffu, mine)) != 1) {
+    const uint32_t w1 = (uint32_t)hi, w2 = (uint32_t)(lo >> 32), w3 = (uint32_t)lo;
+    const uint32_t m1 = __reduce_min_sync(0xffffffffu, mine ? w1 : 0xffffffffu);
+    mine = mine && w1 == m1;
+    const uint32_t m2 = __reduce_min_sync(0xffffffffu, mine ? w2 : 0xffffffffu);
+    mine = mine && w2 == m2;
+    const uint32_t m3 = __reduce_min_sync(0xffffffffu, mine ? w3 : 0xffffffffu);
+    mine = mine && w3 == m3;
   }
   live = __ballot_sync(0xffffffffu, mine);
   if (live == 0) return -1;
