@@ -801,8 +801,9 @@ __global__ void __launch_bounds__(32) build_tree_kernel(const TreeArgs a) {
 // (j = position in the parent's child order, z = neg is -0.0). Candidates never share (depth,
 // parent, rank), so the bits below rank never decide an order, and (hi, lo) compares exactly like
 // the reference's (neg, depth, parent, rank). A pop is a scan of the lane's slots, a warp arg-min
-// over 64 bits (a second one over lo only on a tie), and an in-register replacement: no
-// shared-memory round trip sits on the pop chain except the neg of the popped node's parent.
+// (one 32-bit reduction over hi's upper word when a single lane holds its minimum, else over all of hi
+// and, on a tie, over lo), and an in-register replacement: no shared-memory round trip sits on the pop
+// chain except the neg of the popped node's parent. The output arrays are written after the last pop.
 __device__ __forceinline__ double key_to_neg(uint64_t hi, uint64_t lo) {
   if (lo & 1ull) return -0.0;
   const uint64_t u = (hi >> 63) ? (hi & 0x7fffffffffffffffull) : ~hi;
